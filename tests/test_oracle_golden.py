@@ -1,0 +1,196 @@
+"""Pin the numpy oracle to the reference (CPU).
+
+* known-answer tests restated from the reference's own suite
+  (prism_infer tests/test_expert_parallel.py:15-43, tests/test_moe.py:55-122);
+* golden fixtures produced by running the reference's modules
+  (``tests/golden/make_golden.py``): single-rank fp32/bf16 blocks, benchmark config 0 at full
+  shape, and W=2 / W=4 gloo expert-parallel runs.
+"""
+import numpy as np
+import pytest
+
+from conftest import load_golden
+from oracle import moe_oracle as O
+from prism_infer_b200 import synthetic
+
+FP32_ATOL, FP32_RTOL = 1e-5, 1e-4          # prism_infer tests/test_moe.py:64
+BF16_MAX_ABS, BF16_MEAN_REL = 2e-2, 1e-2   # bf16 output tolerance of the block contract
+
+
+# ------------------------------------------------------------------ known answers
+
+def test_build_dispatch_plan_golden_vector():
+    # prism_infer tests/test_expert_parallel.py:15-22
+    perm, splits, sleid = O.build_dispatch_plan(np.array([[0, 5], [2, 3]]), 2, 4)
+    assert splits.tolist() == [1, 2, 1, 0]
+    assert perm.tolist() == [0, 2, 3, 1]
+    assert sleid.tolist() == [0, 0, 1, 1]
+
+
+def test_build_dispatch_plan_splits_sum_and_permutation():
+    # prism_infer tests/test_expert_parallel.py:24-32
+    rng = np.random.default_rng(0)
+    T, k, E, W = 7, 3, 8, 4
+    ids = rng.integers(0, E, (T, k))
+    perm, splits, _ = O.build_dispatch_plan(ids, E // W, W)
+    assert int(splits.sum()) == T * k
+    assert sorted(perm.tolist()) == list(range(T * k))
+
+
+def test_combine_weighted_sum_known_answer():
+    # prism_infer tests/test_expert_parallel.py:34-43
+    T, k, H = 2, 2, 3
+    unperm = np.arange(T * k * H, dtype=np.float32).reshape(T * k, H)
+    w = np.array([[0.5, 0.5], [1.0, 0.0]], np.float32)
+    y = O.combine_weighted_sum(unperm, w, T, k, "float32")
+    exp = np.stack([0.5 * unperm[0] + 0.5 * unperm[1], 1.0 * unperm[2] + 0.0 * unperm[3]])
+    np.testing.assert_allclose(y, exp)
+
+
+def test_renorm_weights_sum_to_one():
+    # prism_infer tests/test_moe.py:67-76
+    rng = np.random.default_rng(1)
+    probs = O.softmax_fp32(rng.standard_normal((10, 8)).astype(np.float32))
+    w, _ = O.topk_torch_cuda(probs, 2)
+    np.testing.assert_allclose(O.renorm_weights(w).sum(-1), np.ones(10), atol=1e-5)
+
+
+def test_topk_distinct_values_sorted_descending():
+    rng = np.random.default_rng(2)
+    p = rng.random((50, 40)).astype(np.float32)
+    for k in (1, 2, 5, 8, 13, 32):
+        v, i = O.topk_torch_cuda(p, k)
+        ref = np.argsort(-p, axis=1, kind="stable")[:, :k]
+        assert (i == ref).all()
+        assert (v == np.take_along_axis(p, ref, 1)).all()
+
+
+def test_topk_tie_selection_prefers_lower_index():
+    # values equal to the k-th value are gathered in ascending index order
+    p = np.array([[1, 3, 3, 2, 3]], np.float32)
+    v, i = O.topk_torch_cuda(p, 2)
+    assert sorted(i[0].tolist()) == [1, 2]
+    assert (v == 3).all()
+
+
+def test_bf16_round_ties_to_even():
+    x = np.array([1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8, -2.5, 0.0, np.inf], np.float32)
+    r = O.bf16_round(x)
+    assert r[0] == 1.0 and r[1] == 1.0 + 2 ** -6 and r[2] == -2.5 and r[3] == 0 and r[4] == np.inf
+
+
+# ------------------------------------------------------------------ reference goldens
+
+SINGLE = ["moe_fp32_small", "moe_fp32_norenorm", "moe_fp32_refshape", "moe_fp32_empty_experts",
+          "moe_fp32_single_token", "moe_fp32_multidim", "moe_fp32_k6", "moe_fp32_skew",
+          "moe_bf16_small", "moe_bf16_k8"]
+
+
+def _inputs(g):
+    H, E, I, k = int(g["H"]), int(g["E"]), int(g["I"]), int(g["k"])
+    seed, skew = int(g["seed"]), bool(g["skew"])
+    shape = tuple(int(s) for s in g["shape"])
+    wts = synthetic.make_weights_np(H, E, I, seed, skew=skew, k=k)
+    x = synthetic.make_hidden_np(int(np.prod(shape)), H, seed, skew=skew).reshape(*shape, H)
+    if "x" in g:
+        assert np.array_equal(g["x"], x), "synthetic generator drifted from the fixture"
+    return x, wts
+
+
+def _has_tie(row_vals):
+    return len(np.unique(row_vals)) < len(row_vals)
+
+
+@pytest.mark.parametrize("name", SINGLE)
+def test_single_rank_block_matches_reference(name):
+    g = load_golden(name)
+    x, wts = _inputs(g)
+    dtype, k, renorm = str(g["dtype"]), int(g["k"]), bool(g["renorm"])
+    E = int(g["E"])
+    # routing on the reference's own logits
+    ids, w = O.route(g["logits"].reshape(-1, E), k, renorm, dtype)
+    ref_ids = g["topk_ids"].reshape(-1, k)
+    if dtype == "float32":
+        assert (ids == ref_ids).all()
+        np.testing.assert_allclose(w, g["topk_weights"].reshape(-1, k), rtol=1e-6, atol=1e-7)
+    else:
+        # CPU torch.topk orders ties differently from CUDA; compare selected values and the ids
+        # of tokens whose selection has no tie.
+        probs = O.softmax_fp32(g["logits"].reshape(-1, E))
+        ref_vals = np.take_along_axis(probs, ref_ids, 1)
+        got_vals = np.take_along_axis(probs, ids, 1)
+        assert (np.sort(ref_vals, 1) == np.sort(got_vals, 1)).all()
+        untied = np.array([not _has_tie(np.sort(probs[t])[-k - 1:]) for t in range(len(ids))])
+        assert untied.mean() > 0.5
+        assert (ids[untied] == ref_ids[untied]).all()
+        np.testing.assert_array_equal(w[untied], g["topk_weights"].reshape(-1, k)[untied])
+    # full block from the inputs
+    res = O.moe_forward(x, wts.w_gate, wts.w_gate_up, wts.w_down, k, renorm, dtype,
+                        logits=g["logits"].reshape(-1, E))
+    out, ref = res["out"], g["out"]
+    assert out.shape == ref.shape
+    if dtype == "float32":
+        np.testing.assert_allclose(out, ref, atol=FP32_ATOL, rtol=FP32_RTOL)
+        res2 = O.moe_forward(x, wts.w_gate, wts.w_gate_up, wts.w_down, k, renorm, dtype)
+        assert (res2["topk_ids"] == ref_ids).all()
+        np.testing.assert_allclose(res2["out"], ref, atol=FP32_ATOL, rtol=FP32_RTOL)
+    else:
+        o2, r2 = out.reshape(-1, out.shape[-1])[untied], ref.reshape(-1, ref.shape[-1])[untied]
+        assert np.abs(o2 - r2).max() <= BF16_MAX_ABS
+        assert np.abs(o2 - r2).mean() / np.abs(r2).mean() <= BF16_MEAN_REL
+
+
+def test_empty_experts_counts():
+    g = load_golden("moe_fp32_empty_experts")
+    counts = O.expert_counts(g["topk_ids"], int(g["E"]))
+    assert (counts == 0).sum() > 0 and counts.sum() == g["topk_ids"].size
+
+
+def test_config0_full_shape_matches_reference():
+    """Benchmark config 0 (T=256, H=2048, E=128, k=8, I=768, fp32) end to end."""
+    g = load_golden("cfg0")
+    H, E, I, k = int(g["H"]), int(g["E"]), int(g["I"]), int(g["k"])
+    seed = int(g["seed"])
+    wts = synthetic.make_weights_np(H, E, I, seed)
+    x = synthetic.make_hidden_np(int(g["shape"][0]), H, seed)
+    res = O.moe_forward(x, wts.w_gate, wts.w_gate_up, wts.w_down, k, True, "float32")
+    assert (res["topk_ids"] == g["topk_ids"]).all()
+    np.testing.assert_allclose(res["topk_weights"], g["topk_weights"], rtol=1e-5, atol=1e-7)
+    np.testing.assert_allclose(res["out"][:16], g["out_rows"], atol=FP32_ATOL, rtol=FP32_RTOL)
+    np.testing.assert_allclose(res["out"].sum(1), g["out_row_sums"], atol=1e-3, rtol=1e-4)
+    np.testing.assert_allclose(np.abs(res["out"]).sum(1), g["out_abs_sums"], rtol=1e-5)
+
+
+# ------------------------------------------------------------------ expert parallel goldens
+
+@pytest.mark.parametrize("name", ["ep2_fp32", "ep4_fp32", "ep4_tiny", "ep2_bf16"])
+def test_expert_parallel_matches_reference(name):
+    g = load_golden(name)
+    W, H, E, k, I = (int(g[n]) for n in ("W", "H", "E", "k", "I"))
+    dtype, seed = str(g["dtype"]), int(g["seed"])
+    wts = synthetic.make_weights_np(H, E, I, seed)
+    xs = [g[f"r{r}_x"] for r in range(W)]
+    for r in range(W):
+        assert np.array_equal(xs[r], synthetic.make_hidden_np(len(xs[r]), H, seed + 100 * (r + 1)))
+    logits = [g[f"r{r}_logits"] for r in range(W)]
+    ranks = O.ep_forward_all_ranks(xs, wts.w_gate, wts.w_gate_up, wts.w_down, k, True, dtype,
+                                   logits=logits)
+    for r in range(W):
+        R = ranks[r]
+        ref_ids = g[f"r{r}_topk_ids"]
+        if dtype == "float32":
+            assert (R["topk_ids"] == ref_ids).all()
+        # the dispatch plan is integer work: bit-exact on the reference's routing
+        perm, splits, sleid = O.build_dispatch_plan(ref_ids, E // W, W)
+        assert (perm == g[f"r{r}_perm"]).all()
+        assert (splits == g[f"r{r}_input_splits"]).all()
+        assert (sleid == g[f"r{r}_sorted_local_eid"]).all()
+        if dtype == "float32":
+            assert (R["perm"] == g[f"r{r}_perm"]).all()
+            assert (R["output_splits"] == g[f"r{r}_output_splits"]).all()
+            assert (R["recv_eid"] == g[f"r{r}_recv_eid"]).all()
+            np.testing.assert_allclose(R["out"], g[f"r{r}_out"], atol=FP32_ATOL, rtol=FP32_RTOL)
+        else:
+            d = np.abs(R["out"] - g[f"r{r}_out"])
+            assert d.max() <= BF16_MAX_ABS
+            assert d.mean() / np.abs(g[f"r{r}_out"]).mean() <= BF16_MEAN_REL
