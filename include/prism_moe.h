@@ -1,0 +1,173 @@
+/*
+ * prism_moe.h — C ABI of the B200-native (sm_100a) Qwen3-MoE sparse block.
+ *
+ * Library: libprism_moe.so (built from prism_infer_b200/csrc by prism_infer_b200/build.py).
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream (``void*`` holding a
+ * cudaStream_t; NULL = legacy default stream), launches asynchronously on that stream and
+ * returns an ``int`` status (PRISM_MOE_OK = 0). Nothing here allocates device memory: the
+ * caller owns every buffer, including the workspaces sized by the *_workspace_size helpers.
+ * On a non-zero status, prism_moe_last_error() returns a message (thread-local).
+ *
+ * Kernels never trap. Waits inside kernels are bounded; a wait that runs out records
+ * PRISM_MOE_ERR_TIMEOUT in a device error word that the host reads back with
+ * prism_moe_read_device_error().
+ *
+ * Element types: PRISM_MOE_F32 (float) or PRISM_MOE_BF16 (bfloat16, IEEE bit layout, the
+ * upper half of a float). Index outputs that the reference returns as torch.int64 are int64.
+ *
+ * The reference this ABI replaces is pure PyTorch; each function names the reference code
+ * (path:line within SparkSnail/prism-infer) whose behaviour it reproduces.
+ */
+#ifndef PRISM_MOE_H_
+#define PRISM_MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PRISM_MOE_OK 0
+#define PRISM_MOE_ERR_ARG 1          /* invalid argument (shape, dtype, null pointer, size)   */
+#define PRISM_MOE_ERR_CUDA 2         /* a CUDA runtime / driver call failed                    */
+#define PRISM_MOE_ERR_TIMEOUT 3      /* a bounded in-kernel wait ran out                       */
+#define PRISM_MOE_ERR_UNSUPPORTED 4  /* shape or device outside what the kernels implement     */
+#define PRISM_MOE_ERR_DEVICE 5       /* a kernel recorded an error in its device error word    */
+
+#define PRISM_MOE_F32 0
+#define PRISM_MOE_BF16 1
+
+/* Library version (major*10000 + minor*100 + patch). */
+int prism_moe_version(void);
+
+/* Message describing the last non-zero status returned on this thread. */
+const char* prism_moe_last_error(void);
+
+/*
+ * Router post-processing of one MoE block: fp32 softmax over the experts, top-k, optional
+ * renormalisation of the k weights, cast of the weights to the logits' dtype.
+ * Replaces prism_infer/layers/moe.py:77-81 (F.softmax(dtype=float) -> torch.topk -> /sum ->
+ * .to(dtype)), reproducing torch's CUDA results bit for bit: the softmax sums in the order of
+ * torch's warp softmax, top-k resolves ties as torch.topk on CUDA does (values equal to the
+ * k-th are taken in ascending expert index, output order from torch's 32-wide bitonic sort),
+ * and the renormalisation sum follows torch's reduction tree.
+ *   logits        [T, E] row-major, dtype
+ *   topk_ids      [T, k] int64 out
+ *   topk_weights  [T, k] dtype out
+ *   expert_counts [E] int32 out, or NULL (rows routed to each expert; zeroed first)
+ * Limits: 1 <= E <= 1024, 1 <= k <= min(E, 32).
+ */
+int prism_moe_route_topk(const void* logits, int dtype, int64_t num_tokens, int32_t num_experts,
+                         int32_t top_k, int32_t renorm, int64_t* topk_ids, void* topk_weights,
+                         int32_t* expert_counts, void* stream);
+
+/* Bytes of scratch prism_moe_build_dispatch_plan needs. */
+size_t prism_moe_dispatch_workspace_size(int64_t num_tokens, int32_t top_k, int32_t num_experts,
+                                         int32_t ep_size);
+
+/*
+ * Dispatch plan of the routed entries (flat index f = t*k + j), by a deterministic counting
+ * sort. Replaces prism_infer/engine/parallel/expert_parallel.py:23-42 (build_dispatch_plan:
+ * dst = id // E_l, perm = stable argsort(dst), input_splits = bincount(dst),
+ * sorted_local_eid = (id % E_l)[perm]) and the per-expert grouping of
+ * prism_infer/layers/moe.py:91-93. Outputs (each may be NULL if not wanted):
+ *   perm             [T*k] int64  — identical to the reference's perm
+ *   input_splits     [W]   int64  — rows sent to each EP rank
+ *   sorted_local_eid [T*k] int64  — local expert id of perm's entries
+ *   expert_counts    [E]   int32  — rows per expert
+ *   expert_offsets   [E+1] int32  — exclusive scan of expert_counts
+ *   entry_row        [T*k] int32  — row of entry f in expert-major order (experts ascending,
+ *                                   flat order inside an expert); the layout the expert GEMMs
+ *                                   and the EP send buffer use.
+ * Requires num_experts % ep_size == 0 (the reference asserts the same,
+ * expert_parallel.py:103).
+ */
+int prism_moe_build_dispatch_plan(const int64_t* topk_ids, int64_t num_tokens, int32_t top_k,
+                                  int32_t num_experts, int32_t ep_size, int64_t* perm,
+                                  int64_t* input_splits, int64_t* sorted_local_eid,
+                                  int32_t* expert_counts, int32_t* expert_offsets,
+                                  int32_t* entry_row, void* workspace, size_t workspace_bytes,
+                                  void* stream);
+
+/*
+ * Gather token rows into expert-major order: x_sorted[entry_row[t*k + j]] = x[t].
+ * Replaces prism_infer/engine/parallel/expert_parallel.py:154-156 (repeat_interleave + [perm])
+ * and the per-expert x[token_idx] gathers of prism_infer/layers/moe.py:96. 16-byte vector
+ * copies; rows must be 16-byte aligned (hidden * sizeof(dtype) % 16 == 0).
+ */
+int prism_moe_permute_rows(const void* x, int dtype, int64_t num_tokens, int64_t hidden,
+                           int32_t top_k, const int32_t* entry_row, void* x_sorted, void* stream);
+
+/* Bytes of scratch prism_moe_expert_swiglu needs for rows_capacity rows. */
+size_t prism_moe_expert_workspace_size(int64_t rows_capacity, int64_t hidden, int64_t inter,
+                                       int dtype);
+
+/*
+ * Grouped SwiGLU experts: for every segment s, rows [seg_offsets[s], seg_offsets[s+1]) of
+ * x_sorted go through expert e = seg_expert[s] (or e = s when seg_expert is NULL):
+ *   y = (silu(x Wg_e^T) * (x Wu_e^T)) Wd_e^T
+ * with w_gate_up[e] = [Wg_e; Wu_e] of shape [2I, H] (gate rows first) and w_down[e] [H, I].
+ * Replaces prism_infer/layers/moe.py:27-28 with activation.py:8-11, run per expert by the loops
+ * of moe.py:92-96 and expert_parallel.py:165-169. bf16 runs on tcgen05 tensor cores (fp32
+ * accumulation in TMEM, TMA-fed, SwiGLU fused into the first GEMM's epilogue); f32 runs on
+ * CUDA cores in fp32. The intermediate gate/up values and the activation are rounded to
+ * dtype where the reference materialises them.
+ *   seg_offsets   [num_segments+1] int32, device, non-decreasing, last <= rows_capacity
+ *   device_error  int32 device word, or NULL; a kernel that fails records its status there
+ * Rows of x_sorted/y beyond the last segment are not touched. bf16 needs hidden % 8 == 0 and
+ * inter % 8 == 0.
+ */
+int prism_moe_expert_swiglu(const void* x_sorted, int dtype, int64_t rows_capacity,
+                            int64_t hidden, int64_t inter, const int32_t* seg_offsets,
+                            const int32_t* seg_expert, int32_t num_segments,
+                            int32_t num_local_experts, const void* w_gate_up, const void* w_down,
+                            void* y, void* workspace, size_t workspace_bytes, int* device_error,
+                            void* stream);
+
+/*
+ * Weighted combine: out[t] = sum_j w[t, j] * expert_out[row(t*k + j)], row = entry_row[f]
+ * (identity when entry_row is NULL). Each product is rounded to dtype and the k products are
+ * summed in fp32 in slot order, then rounded once: the numerics of the reference's
+ * combine_weighted_sum. Replaces prism_infer/engine/parallel/expert_parallel.py:45-57 fused
+ * with the un-permute of :173-174, and the index_add_ accumulation of
+ * prism_infer/layers/moe.py:97-98.
+ */
+int prism_moe_combine(const void* expert_out, int dtype, const int32_t* entry_row,
+                      const void* topk_weights, int64_t num_tokens, int32_t top_k, int64_t hidden,
+                      void* out, void* stream);
+
+/* Bytes of scratch prism_moe_block_forward needs. */
+size_t prism_moe_block_workspace_size(int64_t num_tokens, int64_t hidden, int64_t inter,
+                                      int32_t num_experts, int32_t top_k, int dtype);
+
+/*
+ * The whole single-GPU block after the router GEMM: route, plan, gather, grouped SwiGLU
+ * experts, weighted combine. Replaces prism_infer/layers/moe.py:77-100 (the reference computes
+ * router_logits = F.linear(x, W_gate) at moe.py:74 with its BLAS; the caller does the same and
+ * passes the logits here, so routing sees the reference's exact logits).
+ *   x [T, H], router_logits [T, E], w_gate_up [E, 2I, H], w_down [E, H, I], out [T, H]: dtype
+ *   topk_ids [T, k] int64 and topk_weights [T, k] dtype: optional outputs (NULL = not wanted)
+ * The workspace's first 4 bytes are the device error word read by
+ * prism_moe_read_device_error().
+ */
+int prism_moe_block_forward(const void* x, const void* router_logits, int dtype,
+                            int64_t num_tokens, int64_t hidden, int64_t inter,
+                            int32_t num_experts, int32_t top_k, int32_t renorm,
+                            const void* w_gate_up, const void* w_down, void* out,
+                            int64_t* topk_ids, void* topk_weights, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+/*
+ * Synchronise ``stream`` and return the status recorded in a device error word
+ * (PRISM_MOE_OK if none), clearing it. ``device_error`` is the int32 word passed to
+ * prism_moe_expert_swiglu, or the start of a prism_moe_block_forward workspace.
+ */
+int prism_moe_read_device_error(int* device_error, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PRISM_MOE_H_ */

@@ -1,0 +1,126 @@
+"""Expert parallelism for the MoE block — names and behaviour of
+prism_infer/engine/parallel/expert_parallel.py, on B200 kernels.
+
+* ``set_expert_parallel_size`` / ``get_expert_parallel_size`` — process-global EP size
+  (expert_parallel.py:7-16).
+* ``expert_rank`` — contiguous expert ownership ``e // E_l`` (expert_parallel.py:19-20).
+* ``build_dispatch_plan`` — (perm, input_splits, sorted_local_eid), bit-identical to the
+  reference's (expert_parallel.py:23-42), computed by the dispatch-plan kernel.
+* ``combine_weighted_sum`` — the weighted sum over k (expert_parallel.py:45-57) by the combine
+  kernel.
+* ``ExpertParallelMoE`` — experts sharded by rank, tokens exchanged with all-to-all
+  (expert_parallel.py:91-176).
+
+Exchange layout. The reference sends rows in perm order (grouped by destination rank, flat
+order inside) and the receiver regroups them per local expert with boolean masks
+(:165-169). Here rows are sent in expert-major order — destination rank, then local expert, then
+flat order — which is the same rank grouping refined by expert (experts are owned in contiguous
+blocks), so the receiver's buffer is already a list of (source rank, local expert) segments that
+the grouped GEMM consumes directly. The per-expert row sequences are the reference's.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from prism_infer_b200 import capi
+from prism_infer_b200.layers.experts import ExpertBank
+
+_EXPERT_PARALLEL_SIZE = 1
+
+# Kernel entry points used by ExpertParallelMoE. Tests of the distributed host logic on CPU
+# (gloo) substitute an oracle-backed object; the product always uses the CUDA library.
+_KERNELS = capi
+
+
+def set_expert_parallel_size(n: int) -> None:
+    global _EXPERT_PARALLEL_SIZE
+    _EXPERT_PARALLEL_SIZE = n
+
+
+def get_expert_parallel_size() -> int:
+    return _EXPERT_PARALLEL_SIZE
+
+
+def expert_rank(expert_id: int, num_local_experts: int) -> int:
+    return expert_id // num_local_experts
+
+
+def build_dispatch_plan(topk_ids: torch.Tensor, num_local_experts: int, ep_size: int):
+    """(perm [T*k] int64, input_splits [W] int64, sorted_local_eid [T*k] int64) — the
+    reference's plan (expert_parallel.py:23-42), from a deterministic counting sort on the GPU."""
+    plan = _KERNELS.dispatch_plan(topk_ids.contiguous(), num_local_experts * ep_size, ep_size,
+                                  want_perm=True)
+    return plan["perm"], plan["input_splits"], plan["sorted_local_eid"]
+
+
+def combine_weighted_sum(unpermuted: torch.Tensor, topk_weights: torch.Tensor,
+                         num_tokens: int, top_k: int) -> torch.Tensor:
+    """out[t] = sum_k w[t,k] * unpermuted[t*k + k] (expert_parallel.py:45-57)."""
+    assert unpermuted.shape[0] == num_tokens * top_k
+    w = topk_weights.to(unpermuted.dtype).reshape(num_tokens, top_k).contiguous()
+    return _KERNELS.combine(unpermuted.contiguous(), w)
+
+
+class ExpertParallelMoE(ExpertBank):
+    """MoE layer with expert parallelism: experts sharded by rank, tokens routed via
+    all-to-all (dispatch -> local experts -> combine); expert_parallel.py:91-111."""
+
+    _expert_list_name = "local_experts"
+
+    def __init__(self, hidden_size: int, intermediate_size: int, num_experts: int,
+                 ep_size: int, ep_rank: int, group=None):
+        super().__init__()
+        assert num_experts % ep_size == 0, "num_experts must be divisible by ep_size"
+        self.hidden_size = hidden_size
+        self.intermediate_size = intermediate_size
+        self.num_experts = num_experts
+        self.ep_size = ep_size
+        self.ep_rank = ep_rank
+        self.num_local_experts = num_experts // ep_size
+        self.local_expert_base = ep_rank * self.num_local_experts
+        self.group = group
+        self._init_bank(self.num_local_experts, hidden_size, intermediate_size)
+
+    def exchange_plan(self, expert_counts: torch.Tensor):
+        """Counts exchange (expert_parallel.py:113-127), per local expert instead of per rank:
+        recv_counts[s, le] = rows source rank s sends for local expert le. Returns
+        (recv_counts [W, E_l] int32 device, in_splits list, out_splits list)."""
+        W, El = self.ep_size, self.num_local_experts
+        send = expert_counts.to(torch.int32).contiguous()
+        if W == 1:
+            recv = send.clone()
+        else:
+            recv = torch.empty_like(send)
+            dist.all_to_all_single(recv, send, group=self.group)
+        recv = recv.view(W, El)
+        splits = torch.cat([send.view(W, El).sum(1), recv.sum(1)]).tolist()   # one host sync
+        return recv, splits[:W], splits[W:]
+
+    def _all_to_all(self, x: torch.Tensor, out_splits, in_splits) -> torch.Tensor:
+        if self.ep_size == 1:
+            return x.clone()
+        out = x.new_empty((sum(out_splits),) + tuple(x.shape[1:]))
+        dist.all_to_all_single(out, x.contiguous(), out_splits, in_splits, group=self.group)
+        return out
+
+    def forward(self, x: torch.Tensor, topk_ids: torch.Tensor,
+                topk_weights: torch.Tensor) -> torch.Tensor:
+        """x [T, H], topk_ids [T, k] global expert ids, topk_weights [T, k] -> [T, H]
+        (expert_parallel.py:140-176)."""
+        K = _KERNELS
+        T, k = topk_ids.shape
+        W, El = self.ep_size, self.num_local_experts
+        plan = K.dispatch_plan(topk_ids.contiguous(), self.num_experts, W, want_perm=False)
+        entry_row = plan["entry_row"]
+        send_x = K.permute_rows(x.contiguous(), k, entry_row)
+        recv_counts, in_splits, out_splits = self.exchange_plan(plan["expert_counts"])
+        recv_x = self._all_to_all(send_x, out_splits, in_splits)
+        seg_offsets = torch.zeros(W * El + 1, dtype=torch.int32, device=x.device)
+        seg_offsets[1:] = torch.cumsum(recv_counts.reshape(-1), 0)
+        seg_expert = (torch.arange(W * El, dtype=torch.int32, device=x.device) % El).contiguous()
+        recv_y = K.expert_swiglu(recv_x, seg_offsets, self.w_gate_up, self.w_down,
+                                 seg_expert=seg_expert)
+        back = self._all_to_all(recv_y, in_splits, out_splits)
+        w = topk_weights.to(x.dtype).contiguous()
+        return K.combine(back, w, entry_row=entry_row)

@@ -1,0 +1,138 @@
+"""Drop-in for prism_infer/layers/moe.py: the Qwen3-MoE sparse block on B200 kernels.
+
+Same constructor (``MoE(hidden_size, intermediate_size, num_experts, top_k,
+norm_topk_prob=True)``, moe.py:40-67), same parameter names (``gate.weight``,
+``experts.{e}.gate_up_proj.weight``, ``experts.{e}.down_proj.weight``; under expert parallelism
+``ep_moe.local_experts.{le}.*``) and same ``forward(hidden_states) -> Tensor`` of the input's
+shape and dtype (moe.py:69-100). The expert-parallel size is read from the process-global
+``set_expert_parallel_size`` before construction, as in the reference (moe.py:57-61).
+
+Forward, single GPU (EP=1):
+  1. ``router_logits = F.linear(x, gate.weight)`` — the reference's own call (moe.py:74), so the
+     logits are bit-identical to the reference's on the same device;
+  2. ``prism_moe_block_forward`` (C ABI): route (softmax/top-k/renorm, bit-exact with torch on
+     CUDA), dispatch plan, row permutation, grouped SwiGLU experts on tcgen05, weighted combine.
+No host synchronisation happens inside ``forward``; it can be captured in a CUDA graph.
+Only bfloat16 and float32 on an sm_100 device are supported; anything else raises.
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from prism_infer_b200 import capi
+from prism_infer_b200.engine.parallel.expert_parallel import (
+    ExpertParallelMoE,
+    get_expert_parallel_size,
+)
+from prism_infer_b200.layers.experts import ExpertBank
+
+_ws_lock = threading.Lock()
+_workspaces: dict = {}
+
+
+def block_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Per-(device, stream) scratch for ``prism_moe_block_forward``; grows on demand. The first
+    four bytes are the kernels' device error word (kept zero)."""
+    stream = torch.cuda.current_stream(device).cuda_stream
+    key = (device.index, stream)
+    with _ws_lock:
+        ws = _workspaces.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+            _workspaces[key] = ws
+    return ws
+
+
+class ReplicatedGate(nn.Module):
+    """Router weight [E, H] replicated on every rank (reference ReplicatedLinear,
+    prism_infer/layers/linear.py:63-77)."""
+
+    def __init__(self, hidden_size: int, num_experts: int):
+        super().__init__()
+        self.weight = nn.Parameter(torch.empty(num_experts, hidden_size), requires_grad=False)
+        self.weight.weight_loader = lambda param, loaded: param.data.copy_(loaded)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return F.linear(x, self.weight)
+
+
+class MoE(ExpertBank):
+    """Token-choice MoE, Qwen/Mixtral routing: softmax -> top-k -> re-norm (moe.py:31-38)."""
+
+    _expert_list_name = "experts"
+
+    def __init__(self, hidden_size: int, intermediate_size: int, num_experts: int, top_k: int,
+                 norm_topk_prob: bool = True) -> None:
+        super().__init__()
+        self.hidden_size = hidden_size
+        self.intermediate_size = intermediate_size
+        self.num_experts = num_experts
+        self.top_k = top_k
+        self.norm_topk_prob = norm_topk_prob
+        self.gate = ReplicatedGate(hidden_size, num_experts)
+        self.ep_size = get_expert_parallel_size()
+        if self.ep_size > 1:
+            import torch.distributed as dist
+            ep_rank = dist.get_rank() if dist.is_initialized() else 0
+            self.ep_moe = ExpertParallelMoE(hidden_size, intermediate_size, num_experts,
+                                            self.ep_size, ep_rank)
+            self.experts = None
+        else:
+            self.ep_moe = None
+            self._init_bank(num_experts, hidden_size, intermediate_size)
+
+    # ExpertBank hooks are inert when the experts live in ep_moe
+    def _views(self):
+        return self.experts if self.experts is not None else []
+
+    def _apply(self, fn, recurse=True):
+        if self.experts is None:
+            return nn.Module._apply(self, fn, recurse)
+        return super()._apply(fn, recurse)
+
+    def route(self, hidden_states: torch.Tensor):
+        """(router_logits, topk_ids, topk_weights) exactly as moe.py:74-81 computes them."""
+        x = hidden_states.reshape(-1, hidden_states.shape[-1])
+        logits = self.gate(x)
+        ids, w, _ = capi.route_topk(logits.contiguous(), self.top_k, self.norm_topk_prob)
+        return logits, ids, w
+
+    def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
+        orig_shape = hidden_states.shape
+        x = hidden_states.reshape(-1, orig_shape[-1])
+        if not x.is_contiguous():
+            x = x.contiguous()
+        T, H = x.shape
+        if x.dtype != self.gate.weight.dtype:
+            raise RuntimeError(f"hidden_states dtype {x.dtype} != MoE weight dtype "
+                               f"{self.gate.weight.dtype}")
+        logits = self.gate(x)                     # moe.py:74 — cuBLAS, as in the reference
+        if self.ep_size > 1:
+            ids, w, _ = capi.route_topk(logits, self.top_k, self.norm_topk_prob)
+            return self.ep_moe(x, ids, w).view(orig_shape)
+        out = torch.empty_like(x)
+        if T == 0:
+            return out.view(orig_shape)
+        lib = capi.load()
+        dt = capi.dtype_code(x.dtype)
+        nbytes = lib.prism_moe_block_workspace_size(T, H, self.intermediate_size,
+                                                    self.num_experts, self.top_k, dt)
+        ws = block_workspace(x.device, nbytes)
+        capi.check(lib.prism_moe_block_forward(
+            x.data_ptr(), logits.data_ptr(), dt, T, H, self.intermediate_size, self.num_experts,
+            self.top_k, int(bool(self.norm_topk_prob)), self.w_gate_up.data_ptr(),
+            self.w_down.data_ptr(), out.data_ptr(), None, None, ws.data_ptr(), ws.numel(),
+            capi.stream_of(x.device)), "prism_moe_block_forward")
+        return out.view(orig_shape)
+
+    def check_device_error(self, device=None) -> None:
+        """Synchronise and raise if a kernel of the last forward recorded an error."""
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        ws = _workspaces.get((dev.index, stream))
+        if ws is not None:
+            capi.check(capi.read_device_error(ws[:4].view(torch.int32), dev), "MoE kernels")

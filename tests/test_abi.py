@@ -1,0 +1,59 @@
+"""The C-ABI library builds, loads and exports every symbol include/prism_moe.h declares
+(no GPU needed: nothing here launches a kernel)."""
+import ctypes
+import re
+
+import pytest
+
+from prism_infer_b200 import build, capi
+
+
+def declared_functions():
+    text = capi.HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(prism_moe_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return capi.load()
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    for must in ("prism_moe_route_topk", "prism_moe_build_dispatch_plan",
+                 "prism_moe_permute_rows", "prism_moe_expert_swiglu", "prism_moe_combine",
+                 "prism_moe_block_forward"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in prism_moe.h but not exported"
+        assert name in capi._SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_library_exports_nothing_undeclared():
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", str(capi.LIB_PATH)],
+                         capture_output=True, text=True, check=True).stdout
+    exported = {l.split()[-1] for l in out.splitlines() if " T " in l}
+    ours = {s for s in exported if s.startswith("prism_moe_")}
+    assert ours == set(declared_functions())
+
+
+def test_host_side_queries(lib):
+    assert lib.prism_moe_version() >= 100
+    assert lib.prism_moe_block_workspace_size(64, 2048, 768, 128, 8, capi.BF16) > 64 * 8 * 2048 * 2
+    assert lib.prism_moe_dispatch_workspace_size(8192, 8, 128, 8) > 0
+    assert lib.prism_moe_block_workspace_size(-1, 2048, 768, 128, 8, capi.BF16) == 0
+
+
+def test_argument_errors_need_no_gpu(lib):
+    # argument checks run before any device call
+    st = lib.prism_moe_route_topk(None, 7, 4, 8, 2, 1, None, None, None, None)
+    assert st == capi.ERR_ARG and "dtype" in capi.last_error()
+    st = lib.prism_moe_build_dispatch_plan(None, 4, 2, 7, 4, None, None, None, None, None, None,
+                                           None, 0, None)
+    assert st == capi.ERR_ARG and "divisible" in capi.last_error()
