@@ -1,0 +1,418 @@
+"""Benchmark of the Qwen3-MoE sparse block on B200 — one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (every N): benchmark config 2's block — H=2048, E=128 experts, top-8, I=768, bf16 —
+with T=8192 tokens per rank and expert parallelism EP=N (16 experts per rank at N=8): weak
+scaling, per-rank work fixed. One step = one ``MoE.forward`` of the drop-in module (router
+GEMM, routing, dispatch, grouped SwiGLU experts, combine; at N>1 the all-to-all dispatch and
+combine). Inputs: seeded synthetic tensors (no dataset exists for this path).
+
+Reported:
+* ``value``: tokens/s over all ranks, device-timed (CUDA events, barrier + synchronize on both
+  sides, max over ranks), inputs resident in HBM;
+* ``e2e``: the same metric through ``MoE.forward`` with the step's hidden states copied from
+  pinned host memory and the output copied back inside the timed region;
+* ``roofline``: the grouped gate_up GEMM (the dominant kernel), its algorithmic FLOPs per
+  launch over its average event-timed duration, against the measured bf16 peak;
+* ``cpu_baseline``: the numpy oracle (a restatement of the reference's CPU path) on a bounded
+  sample of the same workload, on the host's cores (rank 0, N=1 only);
+* ``decode_cfg1``: config 1 (T=64, single GPU) at N=1, HBM roofline.
+``--impl reference`` times the reference algorithm on the host CPU (the oracle port), rank 0
+only, on a sample of the same workload per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "MoE-block tokens/s (Qwen3-30B-A3B block, EP=N, T=8192/rank)"
+UNIT = "tokens/s"
+CFG = dict(T=8192, H=2048, E=128, k=8, I=768)
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=CFG["T"], help="tokens per rank")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def ncu_traffic():
+    """Per-launch DRAM bytes of the gate_up GEMM from the committed ncu summary, if any."""
+    p = REPO / "profiles" / "ncu_traffic.txt"
+    if not p.exists():
+        return None
+    vals = {}
+    for line in p.read_text().splitlines():
+        if "=" in line and not line.lstrip().startswith("#"):
+            k, v = line.split("=", 1)
+            vals[k.strip()] = v.strip()
+    try:
+        return float(vals["gate_up_cfg2_bytes_per_launch"])
+    except (KeyError, ValueError):
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"prism_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self, gpus):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) not in gpus:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        self.path.unlink(missing_ok=True)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(n):
+    import torch
+    import torch.distributed as dist
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n:
+        raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def build_block(T, world, rank, device, cfg_id=2):
+    import torch
+
+    from prism_infer_b200 import synthetic
+    from prism_infer_b200.engine.parallel import set_expert_parallel_size
+    from prism_infer_b200.layers.moe import MoE
+    H, E, k, I = CFG["H"], CFG["E"], CFG["k"], CFG["I"]
+    seed = synthetic.config_seed(cfg_id)
+    set_expert_parallel_size(world)
+    El = E // world
+    wg, wgu, wd = synthetic.make_weights_torch(H, E, I, seed, torch.bfloat16, device,
+                                               expert_range=(rank * El, (rank + 1) * El))
+    moe = MoE(H, I, E, k).to(device=device, dtype=torch.bfloat16)
+    bank = moe.ep_moe if world > 1 else moe
+    with torch.no_grad():
+        moe.gate.weight.copy_(wg)
+        bank.w_gate_up.copy_(wgu)
+        bank.w_down.copy_(wd)
+    x = synthetic.make_hidden_torch(T, H, synthetic.config_seed(cfg_id, rank), torch.bfloat16,
+                                    device)
+    return moe, x
+
+
+def time_device(fn, steps, warmup, world, nvtx=None):
+    """Device time of ``steps`` calls (ms, max over ranks). ``nvtx`` names an NVTX range around
+    the timed calls (used to select them in an ncu launch list)."""
+    import torch
+    import torch.distributed as dist
+    for _ in range(warmup):
+        fn(-1)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if nvtx:
+        torch.cuda.nvtx.range_push(nvtx)
+    start.record()
+    for i in range(steps):
+        fn(i)
+    end.record()
+    if nvtx:
+        torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def cpu_oracle_rate(sample_tokens, reps, seed=2000):
+    """Tokens/s of the numpy oracle (fp32 restatement of the reference's MoE.forward) on
+    ``sample_tokens`` tokens of the workload, best of ``reps``."""
+    import numpy as np
+
+    from oracle import moe_oracle as O
+    from prism_infer_b200 import synthetic
+    H, E, k, I = CFG["H"], CFG["E"], CFG["k"], CFG["I"]
+    wts = synthetic.make_weights_np(H, E, I, seed)
+    x = synthetic.make_hidden_np(sample_tokens, H, seed)
+    best = math.inf
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        O.moe_forward(x, wts.w_gate, wts.w_gate_up, wts.w_down, k, True, "float32")
+        best = min(best, time.perf_counter() - t0)
+    del np
+    return sample_tokens / best, best
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cores = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    sample = 256
+    from oracle import moe_oracle as O
+    from prism_infer_b200 import synthetic
+    H, E, k, I = CFG["H"], CFG["E"], CFG["k"], CFG["I"]
+    wts = synthetic.make_weights_np(H, E, I, 2000)
+    x = synthetic.make_hidden_np(sample, H, 2000)
+    O.moe_forward(x, wts.w_gate, wts.w_gate_up, wts.w_down, k, True, "float32")   # warm-up
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.moe_forward(x, wts.w_gate, wts.w_gate_up, wts.w_down, k, True, "float32")
+    dt = time.perf_counter() - t0
+    value = sample * args.steps / dt
+    desc = (f"numpy oracle (fp32 restatement of prism_infer MoE.forward, moe.py:69-100) on "
+            f"{sample} tokens of the workload per step, {cores} host threads")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "cfg2 block H=2048 E=128 k=8 I=768 (CPU sample)",
+                   "sample_tokens_per_step": sample, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from prism_infer_b200 import capi
+    rank, world, local = dist_setup(args.gpus)
+    device = torch.device("cuda", local)
+    T = args.tokens
+    H, E, k, I = CFG["H"], CFG["E"], CFG["k"], CFG["I"]
+    moe, x = build_block(T, world, rank, device)
+    peaks, peak_kind = load_peaks()
+
+    # ---- device-resident timing with per-stage events ----
+    steps, warmup = args.steps, args.warmup
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(steps)]
+    for row in ev:
+        for e in row:
+            e.record()
+    torch.cuda.synchronize()
+    out_holder = {}
+
+    def step(i):
+        if i >= 0:
+            capi.set_profile_events(ev[i])
+        with torch.inference_mode():
+            out_holder["y"] = moe(x)
+        if i >= 0:
+            capi.set_profile_events(None)
+
+    sampler = ClockSampler() if rank == 0 else None
+    if sampler:
+        sampler.start()
+    ms = time_device(step, steps, warmup, world, nvtx="prism_timed")
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    gpu_ids = ([int(v) for v in vis.split(",")][:world] if vis and all(
+        v.strip().isdigit() for v in vis.split(",")) else list(range(world)))
+    clocks = sampler.stop(gpu_ids) if sampler else None
+    moe.check_device_error(device) if world == 1 else None
+
+    # per-stage averages (ms) — slots: route, plan, permute, gate_up, down, combine
+    names = ["route", "plan", "permute", "gate_up", "down", "combine"]
+    stage_ms = {}
+    for s, name in enumerate(names):
+        vals = []
+        for row in ev:
+            try:
+                vals.append(row[s].elapsed_time(row[s + 1]))
+            except RuntimeError:
+                pass
+        stage_ms[name] = sum(vals) / len(vals) if vals and world == 1 else None
+    if world > 1:
+        # EP path records only the expert GEMM slots (3..5)
+        g = [row[3].elapsed_time(row[4]) for row in ev]
+        d = [row[4].elapsed_time(row[5]) for row in ev]
+        stage_ms["gate_up"] = sum(g) / len(g)
+        stage_ms["down"] = sum(d) / len(d)
+
+    value = world * T * steps / (ms / 1e3)
+
+    # ---- end to end through MoE.forward with host buffers ----
+    x_host = x.detach().cpu().pin_memory()
+    y_host = torch.empty_like(x_host).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step(_i):
+        x_dev.copy_(x_host, non_blocking=True)
+        with torch.inference_mode():
+            y = moe(x_dev)
+        y_host.copy_(y, non_blocking=True)
+
+    ms_e2e = time_device(e2e_step, steps, max(2, warmup // 2), world)
+    e2e_value = world * T * steps / (ms_e2e / 1e3)
+
+    # ---- roofline of the dominant kernel (gate_up grouped GEMM) ----
+    rows = T * k                       # routed rows per rank (EP: received rows ~ T*k)
+    flops_gate_up = 2.0 * rows * H * (2 * I)
+    gu_ms = stage_ms["gate_up"]
+    achieved = flops_gate_up / (gu_ms / 1e3) / 1e12
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    traffic = ncu_traffic()
+    roofline = {"bound": "tensor", "kernel": "grouped_gemm_sm100_kernel<gate_up>",
+                "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_source": f"{peak_kind} bf16_tflops (burst)",
+                "traffic": traffic,
+                "algorithmic": f"2*{rows}*{H}*{2 * I} = {flops_gate_up:.4g} FLOP per launch"}
+    block_flops = T * world * (2 * H * E + k * 6 * H * I)
+    extra = {
+        "stages_ms": stage_ms,
+        "block_tflops": block_flops * steps / (ms / 1e3) / 1e12 / world,
+        "block_frac_of_peak": block_flops * steps / (ms / 1e3) / 1e12 / world / peak,
+    }
+    hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    if world == 1:
+        el = 2
+        perm_bytes = T * H * el + rows * H * el + rows * 4
+        comb_bytes = rows * H * el + T * H * el + rows * (4 + el)
+        extra["hbm"] = {
+            "permute_gbs": perm_bytes / (stage_ms["permute"] / 1e3) / 1e9,
+            "combine_gbs": comb_bytes / (stage_ms["combine"] / 1e3) / 1e9,
+            "route_gbs": (T * E * el + T * k * (8 + el)) / (stage_ms["route"] / 1e3) / 1e9,
+            "peak_gbs": hbm_peak,
+        }
+
+    # ---- config 1 decode (T=64) at N=1 ----
+    if world == 1 and not args.no_decode:
+        xd = x[:64].contiguous()
+
+        def dec(_i):
+            with torch.inference_mode():
+                moe(xd)
+        ms_dec = time_device(dec, 200, 20, 1)
+        with torch.inference_mode():
+            _, ids, _ = moe.route(xd)
+        n_exp = int(torch.unique(ids).numel())
+        wbytes = n_exp * 3 * H * I * 2
+        t_step = ms_dec / 200 / 1e3
+        extra["decode_cfg1"] = {"tokens": 64, "ms_per_step": ms_dec / 200,
+                                "tokens_per_s": 64 / t_step,
+                                "weight_bytes_per_step": wbytes,
+                                "hbm_gbs": wbytes / t_step / 1e9,
+                                "frac_of_hbm_peak": wbytes / t_step / 1e9 / hbm_peak}
+
+    # ---- CPU baseline (rank 0, N=1) ----
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cores = os.cpu_count() or 1
+        sample = 512
+        rate, best = cpu_oracle_rate(sample, 2)
+        cpu = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"numpy oracle, fp32, {sample} tokens of the workload, best of 2 "
+                         f"({best:.2f} s each), {cores} host threads"}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": ms / steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "cfg2: Qwen3-30B-A3B MoE block H=2048 E=128 top-8 I=768",
+                   "tokens_per_rank": T, "global_batch": T * world, "ep": world,
+                   "parallelism": f"ep{world}",
+                   "l2": "inputs larger than L2: 1.2 GB of expert weights streamed per step"},
+        "roofline": roofline,
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * H * 2,
+                "d2h_bytes_per_step": T * H * 2},
+        "gpu_launches": steps * 8,
+        "clocks": clocks,
+        **extra,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

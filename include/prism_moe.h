@@ -160,6 +160,17 @@ int prism_moe_block_forward(const void* x, const void* router_logits, int dtype,
                             size_t workspace_bytes, void* stream);
 
 /*
+ * Profiling hook: CUDA events (cudaEvent_t handles owned by the caller) that the following
+ * calls on this thread record on their stream at stage boundaries — slot 0 route begin,
+ * 1 dispatch-plan begin, 2 permute begin, 3 gate_up GEMM begin, 4 down GEMM begin, 5 combine
+ * begin, 6 combine end (prism_moe_expert_swiglu records slots 3-5). ``count`` = 0 turns it off.
+ * The reference has no equivalent (it times whole engine steps with host clocks,
+ * prism_infer bench/bench.py:445-452); this exists so a benchmark can time each kernel on the
+ * device inside its timed region.
+ */
+int prism_moe_profile_events(void* const* events, int32_t count);
+
+/*
  * Synchronise ``stream`` and return the status recorded in a device error word
  * (PRISM_MOE_OK if none), clearing it. ``device_error`` is the int32 word passed to
  * prism_moe_expert_swiglu, or the start of a prism_moe_block_forward workspace.

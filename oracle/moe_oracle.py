@@ -20,7 +20,7 @@ Parity pins (what ties this restatement to the reference):
 * the reference's known-answer tests ``tests/test_expert_parallel.py:15-22`` (dispatch plan)
   and ``:34-43`` (weighted combine);
 * on a CUDA host, the torch CUDA ops the reference calls on GPU (``F.softmax`` / ``torch.topk``
-  / ``sum`` / cast) for the tie order of ``torch.topk`` (``tests/test_route_gpu.py``).
+  / ``sum`` / cast) for the tie order of ``torch.topk`` (``tests/test_kernels_gpu.py``).
 
 Numerics modelled:
 
@@ -32,7 +32,7 @@ Numerics modelled:
   greater than the k-th value, then values equal to it in ascending index order, and sorts the
   k gathered pairs with a 32-wide bitonic network (invalid slots sort last). ``topk_torch_cuda``
   emulates exactly that, so tied router probabilities resolve as they do on the GPU.
-* the renormalisation sum over k follows the CUDA reduction's pairwise shuffle tree.
+* the renormalisation sum over k follows torch's CUDA reduction tree (decreasing offsets).
 """
 from __future__ import annotations
 
@@ -183,9 +183,10 @@ def topk_torch_cuda(probs: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
 def renorm_weights(w: np.ndarray) -> np.ndarray:
     """``routing_weights / routing_weights.sum(dim=-1, keepdim=True)`` (moe.py:79-80).
 
-    The sum over k follows the CUDA reduction of a short contiguous row: lane ``j`` of a
-    ``last_pow2(k)``-wide group sums elements ``j, j+width, ...`` serially, then lanes combine
-    pairwise (offset 1, 2, 4, ...).
+    The sum over k follows torch's CUDA reduction of a short contiguous row
+    (ATen/native/cuda/Reduce.cuh, torch 2.11): lane ``j`` of a ``last_pow2(k)``-wide group sums
+    elements ``j, j+width, ...`` serially, then lanes combine by shuffle-down with decreasing
+    offsets ``width/2, ..., 2, 1``; for k=8 that is ``((w0+w4)+(w2+w6)) + ((w1+w5)+(w3+w7))``.
     """
     w = np.asarray(w, np.float32)
     T, k = w.shape
@@ -195,14 +196,14 @@ def renorm_weights(w: np.ndarray) -> np.ndarray:
     lanes = np.zeros((T, width), np.float32)
     for j in range(k):
         lanes[:, j % width] = (lanes[:, j % width] + w[:, j]).astype(np.float32)
-    off = 1
-    while off < width:
+    off = width // 2
+    while off > 0:
         nxt = lanes.copy()
         for l in range(width):
             if l + off < width:
                 nxt[:, l] = (lanes[:, l] + lanes[:, l + off]).astype(np.float32)
         lanes = nxt
-        off *= 2
+        off //= 2
     s = lanes[:, 0]
     return (w / s[:, None]).astype(np.float32)
 

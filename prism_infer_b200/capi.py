@@ -40,6 +40,7 @@ _SIGNATURES = {
     "prism_moe_block_forward": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _i64, _i64, _i64, _i32,
                                                _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
                                                _vp]),
+    "prism_moe_profile_events": (ctypes.c_int, [ctypes.POINTER(_vp), _i32]),
     "prism_moe_read_device_error": (ctypes.c_int, [_vp, _vp]),
 }
 
@@ -208,6 +209,14 @@ def combine(expert_out, topk_weights, entry_row=None, out=None):
                                    ptr(topk_weights), T, k, H, ptr(out),
                                    stream_of(expert_out.device)), "prism_moe_combine")
     return out
+
+
+def set_profile_events(events) -> None:
+    """Record ``events`` (torch.cuda.Event, already created) at the kernels' stage boundaries on
+    this thread; ``None`` or an empty list turns the hook off."""
+    events = list(events or [])
+    arr = (_vp * max(len(events), 1))(*[ctypes.c_void_p(e.cuda_event) for e in events])
+    check(load().prism_moe_profile_events(arr, len(events)), "prism_moe_profile_events")
 
 
 def read_device_error(word, device=None) -> int:

@@ -19,7 +19,7 @@ int permute_rows(const void* x, int64_t T, int64_t row_bytes, int k, const int32
 int expert_swiglu_bf16(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
                        const int32_t* seg_offsets, const int32_t* seg_expert, int nseg, int El,
                        const void* wgu, const void* wd, void* y, void* h, int* err,
-                       cudaStream_t st);
+                       cudaStream_t st);  // records stage slots 3, 4, 5
 int expert_swiglu_f32(const float* x, int64_t rows_cap, int64_t H, int64_t I,
                       const int32_t* seg_offsets, const int32_t* seg_expert, int nseg, int El,
                       const float* wgu, const float* wd, float* y, float* h, cudaStream_t st);
@@ -28,6 +28,12 @@ int combine(const void* y, int dtype, const int32_t* entry_row, const void* w, i
 
 namespace {
 thread_local char g_err[512] = "";
+thread_local cudaEvent_t g_stage_events[kNumStageEvents] = {};
+thread_local int g_num_stage_events = 0;
+}
+
+void record_stage(int slot, cudaStream_t st) {
+  if (slot < g_num_stage_events && g_stage_events[slot]) cudaEventRecord(g_stage_events[slot], st);
 }
 
 void set_error(const char* fmt, ...) {
@@ -242,11 +248,14 @@ int prism_moe_block_forward(const void* x, const void* router_logits, int dtype,
   void* h = ws + L.h;
   void* y = ws + L.y;
   const int64_t N = num_tokens * top_k;
+  record_stage(0, st);
   int r = route_topk(router_logits, dtype, num_tokens, num_experts, top_k, renorm, ids, w, nullptr, st);
   if (r) return r;
+  record_stage(1, st);
   r = build_plan(ids, num_tokens, top_k, num_experts, 1, nullptr, nullptr, nullptr, counts, offsets,
                  entry_row, ws + L.plan, L.plan_bytes, st);
   if (r) return r;
+  record_stage(2, st);
   r = permute_rows(x, num_tokens, hidden * elem_size(dtype), top_k, entry_row, xs, st);
   if (r) return r;
   if (dtype == PRISM_MOE_BF16)
@@ -258,7 +267,19 @@ int prism_moe_block_forward(const void* x, const void* router_logits, int dtype,
                           static_cast<const float*>(w_down), static_cast<float*>(y),
                           static_cast<float*>(h), st);
   if (r) return r;
-  return combine(y, dtype, entry_row, w, num_tokens, top_k, hidden, out, st);
+  r = combine(y, dtype, entry_row, w, num_tokens, top_k, hidden, out, st);
+  record_stage(6, st);
+  return r;
+}
+
+int prism_moe_profile_events(void* const* events, int32_t count) {
+  PRISM_CHECK_ARG(count >= 0 && count <= kNumStageEvents, "profile_events: count %d outside [0, %d]",
+                  count, kNumStageEvents);
+  PRISM_CHECK_ARG(count == 0 || events != nullptr, "profile_events: null events");
+  for (int i = 0; i < kNumStageEvents; ++i)
+    g_stage_events[i] = i < count ? static_cast<cudaEvent_t>(events[i]) : nullptr;
+  g_num_stage_events = count;
+  return PRISM_MOE_OK;
 }
 
 int prism_moe_read_device_error(int* device_error, void* stream) {

@@ -45,6 +45,12 @@ inline size_t align_up(size_t a, size_t b) { return (a + b - 1) / b * b; }
 
 int num_sms();
 
+// Optional profiling hook (prism_moe_profile_events): CUDA events recorded on the launching
+// stream at stage boundaries. Slots: 0 route begin, 1 plan begin, 2 permute begin,
+// 3 gate_up begin, 4 down begin, 5 combine begin, 6 combine end.
+constexpr int kNumStageEvents = 7;
+void record_stage(int slot, cudaStream_t st);
+
 // ---------------------------------------------------------------------------------------------
 // device helpers
 // ---------------------------------------------------------------------------------------------

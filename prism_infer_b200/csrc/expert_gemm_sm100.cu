@@ -385,11 +385,15 @@ int expert_swiglu_bf16(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
     int r = encode_bf16_map(&b2, wd, 3, dims, strides, box);
     if (r) return r;
   }
+  record_stage(3, st);
   int r = launch_gemm<kGateUp>(a1, b1, seg_offsets, seg_expert, nseg, rows_cap, H, I,
                                static_cast<uint16_t*>(h), err, st);
   if (r) return r;
-  return launch_gemm<kDown>(a2, b2, seg_offsets, seg_expert, nseg, rows_cap, I, H,
-                            static_cast<uint16_t*>(y), err, st);
+  record_stage(4, st);
+  r = launch_gemm<kDown>(a2, b2, seg_offsets, seg_expert, nseg, rows_cap, I, H,
+                         static_cast<uint16_t*>(y), err, st);
+  record_stage(5, st);
+  return r;
 }
 
 }  // namespace prism

@@ -8,7 +8,8 @@
 //     the k gathered pairs are ordered by the same 32-wide bitonic compare-exchange network
 //     torch applies to top-k outputs, invalid slots sinking to the end;
 //   * renorm: lane j of a last_pow2(k)-wide group sums w[j], w[j+width], ..., then lanes
-//     combine with offsets 1, 2, 4, ...; w / sum; cast with round-to-nearest-even.
+//     combine by shuffle-down with offsets width/2, ..., 2, 1 (torch's intra-warp reduction
+//     order on CUDA); w / sum; cast with round-to-nearest-even.
 #include "common.cuh"
 
 namespace prism {
@@ -162,7 +163,7 @@ __global__ void __launch_bounds__(32 * kRouteWarps)
       const float kj = __shfl_sync(0xffffffffu, key, j);
       if (lane < rw && (j % rw) == lane) acc += kj;
     }
-    for (int off = 1; off < rw; off <<= 1) acc += __shfl_down_sync(0xffffffffu, acc, off);
+    for (int off = rw >> 1; off > 0; off >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, off);
     const float sum = __shfl_sync(0xffffffffu, acc, 0);
     w = key / sum;
   }
