@@ -92,6 +92,25 @@ int prism_moe_build_dispatch_plan(const int64_t* topk_ids, int64_t num_tokens, i
                                   void* stream);
 
 /*
+ * prism_moe_build_dispatch_plan without a workspace argument, for callers that cannot allocate
+ * device memory (a plugin called from a host framework's execute/enqueue callback that only
+ * hands over buffers it owns, or an embedded runtime whose device memory all belongs to its
+ * own pool). This entry point has no counterpart in the reference. Its scratch is a fixed
+ * 768 KiB __device__ array inside the library (held by every GPU that loads the library until
+ * the process exits); outputs are those of prism_moe_build_dispatch_plan, bit for bit.
+ * Limits: num_tokens * top_k <= 65536, num_experts <= 256, ep_size <= 64 — larger problems
+ * return PRISM_MOE_ERR_ARG. The first call on a device looks up the array's address on that
+ * device (make it before any stream capture starts). Calls share the array: calls whose
+ * kernels may overlap on the GPU race and must be serialised. Allocates nothing.
+ */
+int prism_moe_build_dispatch_plan_static(const int64_t* topk_ids, int64_t num_tokens,
+                                         int32_t top_k, int32_t num_experts, int32_t ep_size,
+                                         int64_t* perm, int64_t* input_splits,
+                                         int64_t* sorted_local_eid, int32_t* expert_counts,
+                                         int32_t* expert_offsets, int32_t* entry_row,
+                                         void* stream);
+
+/*
  * Gather token rows into expert-major order: x_sorted[entry_row[t*k + j]] = x[t].
  * Replaces prism_infer/engine/parallel/expert_parallel.py:154-156 (repeat_interleave + [perm])
  * and the per-expert x[token_idx] gathers of prism_infer/layers/moe.py:96. 16-byte vector

@@ -29,6 +29,8 @@ _SIGNATURES = {
     "prism_moe_dispatch_workspace_size": (_sz, [_i64, _i32, _i32, _i32]),
     "prism_moe_build_dispatch_plan": (ctypes.c_int, [_vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp,
                                                      _vp, _vp, _vp, _vp, _sz, _vp]),
+    "prism_moe_build_dispatch_plan_static": (ctypes.c_int, [_vp, _i64, _i32, _i32, _i32, _vp,
+                                                            _vp, _vp, _vp, _vp, _vp, _vp]),
     "prism_moe_permute_rows": (ctypes.c_int, [_vp, ctypes.c_int, _i64, _i64, _i32, _vp, _vp,
                                               _vp]),
     "prism_moe_expert_workspace_size": (_sz, [_i64, _i64, _i64, ctypes.c_int]),
