@@ -96,7 +96,7 @@ int prism_moe_build_dispatch_plan(const int64_t* topk_ids, int64_t num_tokens, i
  * device memory (a plugin called from a host framework's execute/enqueue callback that only
  * hands over buffers it owns, or an embedded runtime whose device memory all belongs to its
  * own pool). This entry point has no counterpart in the reference. Its scratch is a fixed
- * 768 KiB __device__ array inside the library (held by every GPU that loads the library until
+ * 1 MiB __device__ array inside the library (held by every GPU that loads the library until
  * the process exits); outputs are those of prism_moe_build_dispatch_plan, bit for bit.
  * Limits: num_tokens * top_k <= 65536, num_experts <= 256, ep_size <= 64 — larger problems
  * return PRISM_MOE_ERR_ARG. The first call on a device looks up the array's address on that

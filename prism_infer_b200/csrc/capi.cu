@@ -4,27 +4,9 @@
 #include <cstring>
 
 #include "common.cuh"
+#include "internal.h"
 
 namespace prism {
-
-// kernels implemented in the other translation units
-int route_topk(const void* logits, int dtype, int64_t T, int E, int k, int renorm, int64_t* ids,
-               void* w, int32_t* counts, cudaStream_t st);
-size_t dispatch_workspace_size(int64_t N, int E, int W);
-int build_plan(const int64_t* ids, int64_t T, int k, int E, int W, int64_t* perm, int64_t* splits,
-               int64_t* sorted_leid, int32_t* counts, int32_t* offsets, int32_t* entry_row,
-               void* ws, size_t ws_bytes, cudaStream_t st);
-int permute_rows(const void* x, int64_t T, int64_t row_bytes, int k, const int32_t* entry_row,
-                 void* xs, cudaStream_t st);
-int expert_swiglu_bf16(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
-                       const int32_t* seg_offsets, const int32_t* seg_expert, int nseg, int El,
-                       const void* wgu, const void* wd, void* y, void* h, int* err,
-                       cudaStream_t st);  // records stage slots 3, 4, 5
-int expert_swiglu_f32(const float* x, int64_t rows_cap, int64_t H, int64_t I,
-                      const int32_t* seg_offsets, const int32_t* seg_expert, int nseg, int El,
-                      const float* wgu, const float* wd, float* y, float* h, cudaStream_t st);
-int combine(const void* y, int dtype, const int32_t* entry_row, const void* w, int64_t T, int k,
-            int64_t hidden, void* out, cudaStream_t st);
 
 namespace {
 thread_local char g_err[512] = "";
@@ -148,8 +130,8 @@ int prism_moe_build_dispatch_plan(const int64_t* topk_ids, int64_t num_tokens, i
   PRISM_CHECK_ARG(num_tokens == 0 || (topk_ids && workspace), "build_dispatch_plan: null pointer");
   if (int r = check_device()) return r;
   return build_plan(topk_ids, num_tokens, top_k, num_experts, ep_size, perm, input_splits,
-                    sorted_local_eid, expert_counts, expert_offsets, entry_row, workspace,
-                    workspace_bytes, static_cast<cudaStream_t>(stream));
+                    sorted_local_eid, expert_counts, expert_offsets, entry_row, nullptr,
+                    workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 int prism_moe_permute_rows(const void* x, int dtype, int64_t num_tokens, int64_t hidden,
@@ -253,7 +235,7 @@ int prism_moe_block_forward(const void* x, const void* router_logits, int dtype,
   if (r) return r;
   record_stage(1, st);
   r = build_plan(ids, num_tokens, top_k, num_experts, 1, nullptr, nullptr, nullptr, counts, offsets,
-                 entry_row, ws + L.plan, L.plan_bytes, st);
+                 entry_row, nullptr, ws + L.plan, L.plan_bytes, st);
   if (r) return r;
   record_stage(2, st);
   r = permute_rows(x, num_tokens, hidden * elem_size(dtype), top_k, entry_row, xs, st);

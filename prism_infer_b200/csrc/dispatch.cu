@@ -4,14 +4,19 @@
 //   * expert-major: experts ascending, flat order inside an expert (the GEMM / send layout);
 //   * dst-rank-major: EP ranks ascending, flat order inside a rank — exactly the reference's
 //     perm = argsort(id // E_l, stable=True) (expert_parallel.py:37-39).
-// Three launches: per-chunk stable ranks + histograms (one warp per key kind, __match_any),
-// a column scan of the histograms, and a scatter that writes every output.
+// Three launches:
+//   1. plan_chunk: per chunk of 256 entries (ids staged in shared memory), stable ranks inside
+//      the chunk by expert (warp 0) and by destination rank (warp 1) with __match_any_sync,
+//      and the chunk's histograms;
+//   2. plan_scan: one CTA turns the [chunk][key] histograms into per-chunk bases (each key's
+//      column split across up to 1024/keys threads, two passes) and the key offsets;
+//   3. plan_scatter: every output (entry_row, row_entry, perm, sorted_local_eid).
 #include "common.cuh"
 
 namespace prism {
 namespace {
 
-constexpr int kChunk = 512;   // entries per chunk
+constexpr int kChunk = 256;   // entries per chunk
 constexpr int kMaxKeys = 1024;
 
 __device__ __forceinline__ uint32_t lanemask_lt() {
@@ -20,21 +25,27 @@ __device__ __forceinline__ uint32_t lanemask_lt() {
   return m;
 }
 
-// warp 0 ranks entries by expert, warp 1 by destination rank (if wanted).
 __global__ void __launch_bounds__(64)
     plan_chunk_kernel(const int64_t* __restrict__ ids, int64_t N, int E, int El, int W,
                       int32_t* __restrict__ rank_e, int32_t* __restrict__ rank_d,
                       int32_t* __restrict__ hist_e, int32_t* __restrict__ hist_d,
                       int* __restrict__ err) {
   __shared__ int32_t cnt[2][kMaxKeys];
+  __shared__ int32_t key_s[kChunk];
+  const int64_t c0 = static_cast<int64_t>(blockIdx.x) * kChunk;
+  const int n = static_cast<int>(N - c0 < kChunk ? N - c0 : kChunk);
   for (int i = threadIdx.x; i < kMaxKeys; i += blockDim.x) {
     cnt[0][i] = 0;
     cnt[1][i] = 0;
   }
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int64_t e = ids[c0 + i];
+    const bool ok = e >= 0 && e < E;
+    if (!ok) record_device_error(err, PRISM_MOE_ERR_ARG);
+    key_s[i] = ok ? static_cast<int32_t>(e) : -1;
+  }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t c0 = static_cast<int64_t>(blockIdx.x) * kChunk;
-  const int n = static_cast<int>(N - c0 < kChunk ? N - c0 : kChunk);
   if (warp == 0 || rank_d != nullptr) {
     int32_t* my_cnt = cnt[warp];
     int32_t* my_rank = warp == 0 ? rank_e : rank_d;
@@ -42,17 +53,9 @@ __global__ void __launch_bounds__(64)
       const int i = base + lane;
       const bool in = i < n;
       int key = -1 - lane;  // unique non-matching key for idle lanes
-      if (in) {
-        const int64_t e = ids[c0 + i];
-        if (e >= 0 && e < E) {
-          key = warp == 0 ? static_cast<int>(e) : static_cast<int>(e / El);
-        } else if (warp == 0) {
-          record_device_error(err, PRISM_MOE_ERR_ARG);
-        }
-      }
+      if (in && key_s[i] >= 0) key = warp == 0 ? key_s[i] : key_s[i] / El;
       const uint32_t peers = __match_any_sync(0xffffffffu, key);
-      int prior = 0;
-      if (key >= 0) prior = my_cnt[key];
+      const int prior = key >= 0 ? my_cnt[key] : 0;
       __syncwarp();
       if (key >= 0) {
         my_rank[c0 + i] = prior + __popc(peers & lanemask_lt());
@@ -69,11 +72,11 @@ __global__ void __launch_bounds__(64)
     for (int d = threadIdx.x; d < W; d += blockDim.x) hist_d[blockIdx.x * W + d] = cnt[1][d];
 }
 
-// Exclusive block scan of ``vals`` (n <= blockDim.x <= 1024) in shared memory.
+// Exclusive block scan of ``vals`` (n <= blockDim.x == 1024) in shared memory.
 __device__ void block_exclusive_scan(int32_t* vals, int n, int32_t* total) {
   __shared__ int32_t tmp[kMaxKeys];
   const int i = threadIdx.x;
-  int32_t x = i < n ? vals[i] : 0;
+  const int32_t x = i < n ? vals[i] : 0;
   tmp[i] = x;
   __syncthreads();
   for (int off = 1; off < blockDim.x; off <<= 1) {
@@ -87,45 +90,60 @@ __device__ void block_exclusive_scan(int32_t* vals, int n, int32_t* total) {
   __syncthreads();
 }
 
-// Column scans over chunks; totals; exclusive scans over experts / ranks.
+// hist[c][key] (nchunks x nkeys) -> per-chunk exclusive bases in place; totals[key].
+// Thread (part, key): part p of P = 1024 / nkeys scans chunks [p*cpp, (p+1)*cpp).
+__device__ void column_scan(int32_t* __restrict__ hist, int nchunks, int nkeys,
+                            int32_t* totals, int32_t* part_sum) {
+  const int P = kMaxKeys / nkeys;
+  const int key = threadIdx.x % nkeys;
+  const int part = threadIdx.x / nkeys;
+  const int cpp = (nchunks + P - 1) / P;
+  const int lo = part * cpp;
+  const int hi = lo + cpp < nchunks ? lo + cpp : nchunks;
+  int32_t s = 0;
+  if (part < P) {
+#pragma unroll 8
+    for (int c = lo; c < hi; ++c) s += hist[c * nkeys + key];
+    part_sum[part * nkeys + key] = s;
+  }
+  __syncthreads();
+  if (part < P) {
+    int32_t run = 0;
+    for (int q = 0; q < part; ++q) run += part_sum[q * nkeys + key];
+    if (part == 0) {
+      int32_t tot = 0;
+      for (int q = 0; q < P; ++q) tot += part_sum[q * nkeys + key];
+      totals[key] = tot;
+    }
+#pragma unroll 8
+    for (int c = lo; c < hi; ++c) {
+      const int32_t h = hist[c * nkeys + key];
+      hist[c * nkeys + key] = run;
+      run += h;
+    }
+  }
+  __syncthreads();
+}
+
 __global__ void __launch_bounds__(1024)
     plan_scan_kernel(int nchunks, int E, int W, int32_t* __restrict__ hist_e,
                      int32_t* __restrict__ hist_d, int32_t* __restrict__ counts,
                      int32_t* __restrict__ offsets, int32_t* __restrict__ split_off,
                      int64_t* __restrict__ splits64) {
-  __shared__ int32_t tot_e[kMaxKeys];
-  __shared__ int32_t tot_d[kMaxKeys];
+  __shared__ int32_t tot[kMaxKeys];
+  __shared__ int32_t part_sum[kMaxKeys];
   __shared__ int32_t total;
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    int32_t run = 0;
-#pragma unroll 8
-    for (int c = 0; c < nchunks; ++c) {
-      const int32_t h = hist_e[c * E + e];
-      hist_e[c * E + e] = run;  // becomes the chunk's base inside expert e
-      run += h;
-    }
-    tot_e[e] = run;
-    if (counts) counts[e] = run;
-  }
-  if (hist_d) {
-    for (int d = threadIdx.x; d < W; d += blockDim.x) {
-      int32_t run = 0;
-      for (int c = 0; c < nchunks; ++c) {
-        const int32_t h = hist_d[c * W + d];
-        hist_d[c * W + d] = run;
-        run += h;
-      }
-      tot_d[d] = run;
-      if (splits64) splits64[d] = run;
-    }
-  }
-  __syncthreads();
-  block_exclusive_scan(tot_e, E, &total);
-  for (int e = threadIdx.x; e < E; e += blockDim.x) offsets[e] = tot_e[e];
+  column_scan(hist_e, nchunks, E, tot, part_sum);
+  if (threadIdx.x < E && counts) counts[threadIdx.x] = tot[threadIdx.x];
+  block_exclusive_scan(tot, E, &total);
+  if (threadIdx.x < E) offsets[threadIdx.x] = tot[threadIdx.x];
   if (threadIdx.x == 0) offsets[E] = total;
+  __syncthreads();
   if (hist_d) {
-    block_exclusive_scan(tot_d, W, nullptr);
-    for (int d = threadIdx.x; d < W; d += blockDim.x) split_off[d] = tot_d[d];
+    column_scan(hist_d, nchunks, W, tot, part_sum);
+    if (threadIdx.x < W && splits64) splits64[threadIdx.x] = tot[threadIdx.x];
+    block_exclusive_scan(tot, W, nullptr);
+    if (threadIdx.x < W) split_off[threadIdx.x] = tot[threadIdx.x];
   }
 }
 
@@ -136,7 +154,8 @@ __global__ void plan_scatter_kernel(const int64_t* __restrict__ ids, int64_t N, 
                                     const int32_t* __restrict__ base_d,
                                     const int32_t* __restrict__ offsets,
                                     const int32_t* __restrict__ split_off,
-                                    int32_t* __restrict__ entry_row, int64_t* __restrict__ perm,
+                                    int32_t* __restrict__ entry_row,
+                                    int32_t* __restrict__ row_entry, int64_t* __restrict__ perm,
                                     int64_t* __restrict__ sorted_leid) {
   const int64_t f = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (f >= N) return;
@@ -146,7 +165,9 @@ __global__ void plan_scatter_kernel(const int64_t* __restrict__ ids, int64_t N, 
     return;
   }
   const int c = static_cast<int>(f / kChunk);
-  if (entry_row) entry_row[f] = offsets[e] + base_e[c * E + e] + rank_e[f];
+  const int32_t row = offsets[e] + base_e[c * E + e] + rank_e[f];
+  if (entry_row) entry_row[f] = row;
+  if (row_entry) row_entry[row] = static_cast<int32_t>(f);
   if (perm || sorted_leid) {
     const int d = static_cast<int>(e / El);
     const int64_t p = split_off[d] + base_d[c * W + d] + rank_d[f];
@@ -163,10 +184,7 @@ __global__ void permute_rows_kernel(const uint4* __restrict__ x, int64_t T, int6
   const int lane = threadIdx.x & 31;
   const int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   if (t >= T) return;
-  int rows[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j)
-    if (j < k) rows[j] = entry_row[t * k + j];
+  const int my_row = lane < k ? entry_row[t * k + lane] : -1;
   for (int64_t v0 = 0; v0 < vec_per_row; v0 += 32 * kVecPerLane) {
     uint4 buf[kVecPerLane];
 #pragma unroll
@@ -174,10 +192,8 @@ __global__ void permute_rows_kernel(const uint4* __restrict__ x, int64_t T, int6
       const int64_t v = v0 + q * 32 + lane;
       if (v < vec_per_row) buf[q] = x[t * vec_per_row + v];
     }
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      if (j >= k) break;
-      const int r = rows[j];
+    for (int j = 0; j < k; ++j) {
+      const int r = __shfl_sync(0xffffffffu, my_row, j);
       if (r < 0) continue;
 #pragma unroll
       for (int q = 0; q < kVecPerLane; ++q) {
@@ -203,7 +219,8 @@ size_t dispatch_workspace_size(int64_t N, int E, int W) {
 
 int build_plan(const int64_t* ids, int64_t T, int k, int E, int W, int64_t* perm,
                int64_t* splits, int64_t* sorted_leid, int32_t* counts, int32_t* offsets,
-               int32_t* entry_row, void* ws, size_t ws_bytes, cudaStream_t st) {
+               int32_t* entry_row, int32_t* row_entry, void* ws, size_t ws_bytes,
+               cudaStream_t st) {
   const int64_t N = T * k;
   PRISM_CHECK_ARG(E >= 1 && E <= kMaxKeys, "num_experts %d outside [1, %d]", E, kMaxKeys);
   PRISM_CHECK_ARG(W >= 1 && E % W == 0, "num_experts %d not divisible by ep_size %d", E, W);
@@ -242,12 +259,13 @@ int build_plan(const int64_t* ids, int64_t T, int k, int E, int W, int64_t* perm
       ids, N, E, El, W, rank_e, want_d ? rank_d : nullptr, hist_e, want_d ? hist_d : nullptr,
       err);
   PRISM_LAUNCH_CHECK("plan_chunk_kernel launch");
-  plan_scan_kernel<<<1, 1024, 0, st>>>(static_cast<int>(nchunks), E, W, hist_e,
-                                       want_d ? hist_d : nullptr, cnt, off, split_off, splits);
+  plan_scan_kernel<<<1, kMaxKeys, 0, st>>>(static_cast<int>(nchunks), E, W, hist_e,
+                                           want_d ? hist_d : nullptr, cnt, off, split_off,
+                                           splits);
   PRISM_LAUNCH_CHECK("plan_scan_kernel launch");
   plan_scatter_kernel<<<static_cast<unsigned>(ceil_div(N, 256)), 256, 0, st>>>(
-      ids, N, E, El, W, rank_e, rank_d, hist_e, hist_d, off, split_off, entry_row, perm,
-      sorted_leid);
+      ids, N, E, El, W, rank_e, rank_d, hist_e, hist_d, off, split_off, entry_row, row_entry,
+      perm, sorted_leid);
   PRISM_LAUNCH_CHECK("plan_scatter_kernel launch");
   return PRISM_MOE_OK;
 }

@@ -8,7 +8,7 @@
 // fixed size, so the call allocates nothing.
 //
 // Limits (checked; larger problems get PRISM_MOE_ERR_ARG): num_tokens * top_k <= 65536
-// routed entries, num_experts <= 256, ep_size <= 64. The array (768 KiB) is part of the module
+// routed entries, num_experts <= 256, ep_size <= 64. The array (1 MiB) is part of the module
 // image: every GPU that loads the library holds it until the process exits.
 //
 // Set-up: the first call on a device looks up the array's device address with
@@ -20,20 +20,15 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "internal.h"
 
 namespace prism {
-
-size_t dispatch_workspace_size(int64_t N, int E, int W);
-int build_plan(const int64_t* ids, int64_t T, int k, int E, int W, int64_t* perm, int64_t* splits,
-               int64_t* sorted_leid, int32_t* counts, int32_t* offsets, int32_t* entry_row,
-               void* ws, size_t ws_bytes, cudaStream_t st);
-
 namespace {
 
 constexpr int64_t kStaticMaxEntries = 65536;
 constexpr int kStaticMaxExperts = 256;
 constexpr int kStaticMaxEpSize = 64;
-constexpr size_t kStaticScratchBytes = 768 * 1024;
+constexpr size_t kStaticScratchBytes = 1024 * 1024;
 constexpr int kMaxDevices = 64;
 
 // Host code must not use this name as an address: on the host it is only a stand-in symbol.
@@ -94,6 +89,6 @@ extern "C" __attribute__((visibility("default"))) int prism_moe_build_dispatch_p
   // the plan's error word (first bytes of its scratch) must start at zero on every call
   PRISM_CUDA(cudaMemsetAsync(scratch, 0, 256, st));
   return build_plan(topk_ids, num_tokens, top_k, num_experts, ep_size, perm, input_splits,
-                    sorted_local_eid, expert_counts, expert_offsets, entry_row, scratch,
+                    sorted_local_eid, expert_counts, expert_offsets, entry_row, nullptr, scratch,
                     kStaticScratchBytes, st);
 }

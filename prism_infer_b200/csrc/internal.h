@@ -1,0 +1,38 @@
+// Host-side entry points of the kernels, shared by the extern "C" layer (capi.cu,
+// dispatch_static.cu). Every function validates its own launch-specific limits and returns a
+// PRISM_MOE_* status.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace prism {
+
+// route.cu
+int route_topk(const void* logits, int dtype, int64_t T, int E, int k, int renorm, int64_t* ids,
+               void* w, int32_t* counts, cudaStream_t st);
+
+// dispatch.cu — row_entry (row -> flat entry) is an internal output, NULL when not wanted
+size_t dispatch_workspace_size(int64_t N, int E, int W);
+int build_plan(const int64_t* ids, int64_t T, int k, int E, int W, int64_t* perm, int64_t* splits,
+               int64_t* sorted_leid, int32_t* counts, int32_t* offsets, int32_t* entry_row,
+               int32_t* row_entry, void* ws, size_t ws_bytes, cudaStream_t st);
+int permute_rows(const void* x, int64_t T, int64_t row_bytes, int k, const int32_t* entry_row,
+                 void* xs, cudaStream_t st);
+
+// expert_gemm_sm100.cu — records profiling stage slots 3, 4, 5
+int expert_swiglu_bf16(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
+                       const int32_t* seg_offsets, const int32_t* seg_expert, int nseg, int El,
+                       const void* wgu, const void* wd, void* y, void* h, int* err,
+                       cudaStream_t st);
+
+// expert_gemm_simt.cu
+int expert_swiglu_f32(const float* x, int64_t rows_cap, int64_t H, int64_t I,
+                      const int32_t* seg_offsets, const int32_t* seg_expert, int nseg, int El,
+                      const float* wgu, const float* wd, float* y, float* h, cudaStream_t st);
+
+// combine.cu
+int combine(const void* y, int dtype, const int32_t* entry_row, const void* w, int64_t T, int k,
+            int64_t hidden, void* out, cudaStream_t st);
+
+}  // namespace prism

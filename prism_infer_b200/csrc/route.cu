@@ -66,103 +66,114 @@ __global__ void __launch_bounds__(32 * kRouteWarps)
   for (int it = 0; it < EPT; ++it) v[it] = v[it] / s;
 
   // ---- top-k selection: best value first, lowest index among equal values ----
-  uint32_t taken = 0;
+  // Probabilities are >= 0, so their bit patterns order like their values; NaN maps above +inf
+  // (torch.topk ranks NaN highest). Keys are offset by one so that 0 means "nothing left".
+  uint32_t key_u[EPT];
+#pragma unroll
+  for (int it = 0; it < EPT; ++it) {
+    const int idx = lane + 32 * it;
+    key_u[it] = (lane_ok && idx < E) ? (isnan(v[it]) ? 0x7f800001u : __float_as_uint(v[it])) + 1u
+                                     : 0u;
+  }
   float my_v = 0.f;
   int my_i = 0;
+  uint32_t my_key = 0;
   for (int j = 0; j < k; ++j) {
-    float bv = 0.f;
-    int bi = 0x7fffffff;
+    uint32_t best = 0;
+    uint32_t best_i = 0xffffffffu;
 #pragma unroll
     for (int it = 0; it < EPT; ++it) {
-      const int idx = lane + 32 * it;
-      if (lane_ok && idx < E && !((taken >> it) & 1u)) {
-        if (bi == 0x7fffffff || gt_nan(v[it], bv)) {
-          bv = v[it];
-          bi = idx;
-        }
+      if (key_u[it] > best) {   // ascending it: the lowest index wins among equal keys
+        best = key_u[it];
+        best_i = lane + 32 * it;
       }
     }
+    const uint32_t wmax = __reduce_max_sync(0xffffffffu, best);
+    const uint32_t widx = __reduce_min_sync(0xffffffffu, best == wmax ? best_i : 0xffffffffu);
+    if ((widx & 31u) == static_cast<uint32_t>(lane)) {
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-      const bool take =
-          oi != 0x7fffffff &&
-          (bi == 0x7fffffff || gt_nan(ov, bv) || (!gt_nan(bv, ov) && oi < bi));
-      if (take) {
-        bv = ov;
-        bi = oi;
-      }
+      for (int it = 0; it < EPT; ++it)
+        if (static_cast<uint32_t>(lane + 32 * it) == widx) key_u[it] = 0;
     }
-    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
     if (lane == j) {
-      my_v = bv;
-      my_i = bi;
+      my_key = wmax;
+      my_i = static_cast<int>(widx);
     }
   }
-
-  // ---- gather order of torch's top-k: (value > kth) by index, then (value == kth) by index ----
-  const float vk = __shfl_sync(0xffffffffu, my_v, k - 1);
+  // the selected probability itself, from the lane that holds it
+  my_v = __shfl_sync(0xffffffffu, v[0], my_i & 31);
+#pragma unroll
+  for (int it = 1; it < EPT; ++it) {
+    const float o = __shfl_sync(0xffffffffu, v[it], my_i & 31);
+    if ((my_i >> 5) == it) my_v = o;
+  }
   const bool valid = lane < k;
-  const bool is_gt = valid && gt_nan(my_v, vk);
-  const int n_gt = __popc(__ballot_sync(0xffffffffu, is_gt));
-  int gpos = lane;
-  {
-    int r = 0;
-    for (int q = 0; q < n_gt; ++q) {
-      const int oi = __shfl_sync(0xffffffffu, my_i, q);
-      r += (oi < my_i) ? 1 : 0;
-    }
-    if (is_gt) gpos = r;
-  }
-  int src = lane;
-  for (int q = 0; q < k; ++q) {
-    const int g = __shfl_sync(0xffffffffu, gpos, q);
-    if (g == lane) src = q;
-  }
-  float key = __shfl_sync(0xffffffffu, my_v, src);
-  int val = __shfl_sync(0xffffffffu, my_i, src);
-  int ok = valid ? 1 : 0;
+  float key = my_v;
+  int val = my_i;
 
-  // ---- 32-wide bitonic network (descending, invalid last) ----
-  auto cmp_exchange = [&](int stride, bool flag) {
-    const float pk = __shfl_xor_sync(0xffffffffu, key, stride);
-    const int pv = __shfl_xor_sync(0xffffffffu, val, stride);
-    const int pok = __shfl_xor_sync(0xffffffffu, ok, stride);
-    const bool is_lo = (lane & stride) == 0;
-    const float ak = is_lo ? key : pk;
-    const float bk = is_lo ? pk : key;
-    const int aok = is_lo ? ok : pok;
-    const int bok = is_lo ? pok : ok;
-    const bool swap = (gt_nan(ak, bk) && aok) || !bok;
-    if (swap == flag) {
-      key = pk;
-      val = pv;
-      ok = pok;
+  // ---- torch's output order. Distinct values: descending, which the selection already is.
+  // With ties, replay torch: gather (value > kth) by index, then (value == kth) by index, then
+  // its 32-wide bitonic network (descending, invalid slots last).
+  const uint32_t next_key = __shfl_down_sync(0xffffffffu, my_key, 1);
+  const bool has_tie = __any_sync(0xffffffffu, lane < k - 1 && my_key == next_key);
+  if (has_tie) {
+    const float vk = __shfl_sync(0xffffffffu, my_v, k - 1);
+    const bool is_gt = valid && gt_nan(my_v, vk);
+    const int n_gt = __popc(__ballot_sync(0xffffffffu, is_gt));
+    int gpos = lane;
+    {
+      int r = 0;
+      for (int q = 0; q < n_gt; ++q) {
+        const int oi = __shfl_sync(0xffffffffu, my_i, q);
+        r += (oi < my_i) ? 1 : 0;
+      }
+      if (is_gt) gpos = r;
     }
-  };
-#pragma unroll
-  for (int size = 2; size < 32; size <<= 1) {
-#pragma unroll
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      const int lo = lane & ~stride;
-      cmp_exchange(stride, (lo & size) != 0);
+    int src = lane;
+    for (int q = 0; q < k; ++q) {
+      const int g = __shfl_sync(0xffffffffu, gpos, q);
+      if (g == lane) src = q;
     }
+    key = __shfl_sync(0xffffffffu, my_v, src);
+    val = __shfl_sync(0xffffffffu, my_i, src);
+    int ok = valid ? 1 : 0;
+    auto cmp_exchange = [&](int stride, bool flag) {
+      const float pk = __shfl_xor_sync(0xffffffffu, key, stride);
+      const int pv = __shfl_xor_sync(0xffffffffu, val, stride);
+      const int pok = __shfl_xor_sync(0xffffffffu, ok, stride);
+      const bool is_lo = (lane & stride) == 0;
+      const float ak = is_lo ? key : pk;
+      const float bk = is_lo ? pk : key;
+      const int aok = is_lo ? ok : pok;
+      const int bok = is_lo ? pok : ok;
+      const bool swap = (gt_nan(ak, bk) && aok) || !bok;
+      if (swap == flag) {
+        key = pk;
+        val = pv;
+        ok = pok;
+      }
+    };
+#pragma unroll
+    for (int size = 2; size < 32; size <<= 1) {
+#pragma unroll
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        const int lo = lane & ~stride;
+        cmp_exchange(stride, (lo & size) != 0);
+      }
+    }
+#pragma unroll
+    for (int stride = 16; stride > 0; stride >>= 1) cmp_exchange(stride, false);
   }
-#pragma unroll
-  for (int stride = 16; stride > 0; stride >>= 1) cmp_exchange(stride, false);
 
   // ---- renormalisation in torch's reduction order ----
   float w = key;
   if (renorm) {
     int rw = 1;
     while (rw * 2 <= k) rw *= 2;
-    // lane l < rw sums elements l, l+rw, l+2rw, ... in order
+    // lane l < rw holds w[l] (+ w[l+rw] when it exists: rw > k/2, so at most two elements)
+    const float other = __shfl_down_sync(0xffffffffu, key, rw);
     float acc = 0.f;
-    for (int j = 0; j < k; ++j) {
-      const float kj = __shfl_sync(0xffffffffu, key, j);
-      if (lane < rw && (j % rw) == lane) acc += kj;
-    }
+    if (lane < rw) acc = (lane + rw < k) ? key + other : key;
     for (int off = rw >> 1; off > 0; off >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, off);
     const float sum = __shfl_sync(0xffffffffu, acc, 0);
     w = key / sum;
