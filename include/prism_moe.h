@@ -178,6 +178,56 @@ int prism_moe_block_forward(const void* x, const void* router_logits, int dtype,
                             int64_t* topk_ids, void* topk_weights, void* workspace,
                             size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * Expert parallelism over NVLink peer memory (one process per GPU).
+ *
+ * Replaces the reference's NCCL exchange — counts all_to_all + host .tolist() and the three
+ * variable all_to_all_single calls (prism_infer/engine/parallel/expert_parallel.py:113-136,
+ * :157-162, :172) — with device-side exchange: every rank allocates one landing zone, shares it
+ * through CUDA IPC, and each step writes rows straight into the owners' memory. Waits between
+ * ranks are bounded (10 s) and record PRISM_MOE_ERR_TIMEOUT in the workspace's error word.
+ * --------------------------------------------------------------------------------------------- */
+
+/* Bytes of one rank's landing zone for up to ``max_tokens`` tokens per rank (identical on all
+ * ranks: they must pass the same arguments). */
+size_t prism_moe_ep_landing_bytes(int32_t ep_size, int64_t max_tokens, int32_t top_k,
+                                  int64_t hidden, int32_t num_experts, int dtype);
+
+/* Allocate (cudaMalloc) and zero the flag area of a landing zone on the current device, and
+ * write its CUDA IPC handle (prism_moe_ep_ipc_handle_bytes() bytes) to ``ipc_handle``. These
+ * setup calls are the only ones in the library that allocate. */
+int prism_moe_ep_alloc_landing(size_t bytes, void** ptr, void* ipc_handle);
+int prism_moe_ep_free_landing(void* ptr);
+int prism_moe_ep_ipc_handle_bytes(void);
+
+/* Map / unmap a peer rank's landing zone from its IPC handle. */
+int prism_moe_ep_open_peer(const void* ipc_handle, void** ptr);
+int prism_moe_ep_close_peer(void* ptr);
+
+/* Bytes of the per-rank workspace prism_moe_ep_forward needs. */
+size_t prism_moe_ep_workspace_size(int64_t max_tokens, int64_t hidden, int64_t inter,
+                                   int32_t num_experts, int32_t top_k, int32_t ep_size, int dtype);
+
+/*
+ * One expert-parallel MoE block step on this rank (bf16). Replaces
+ * prism_infer/layers/moe.py:77-85 + ExpertParallelMoE.forward
+ * (prism_infer/engine/parallel/expert_parallel.py:140-176). Collective: every rank of the EP
+ * group calls it once per step with the same ``epoch`` (1, 2, 3, ... increasing by one).
+ *   x [T, H], out [T, H]; either router_logits [T, E] (routed here as prism_moe_route_topk) or
+ *   topk_ids [T, k] int64 + topk_weights [T, k].
+ *   w_gate_up [E/W, 2I, H], w_down [E/W, H, I]: this rank's experts e in [rank*E/W, (rank+1)*E/W)
+ *   my_landing: this rank's landing zone; peer_landing: DEVICE array of W uint64 landing-zone
+ *   addresses as mapped in this process (entry ep_rank = my_landing).
+ * T <= max_tokens (the landing capacity).
+ */
+int prism_moe_ep_forward(const void* x, const void* router_logits, const int64_t* topk_ids,
+                         const void* topk_weights, int dtype, int64_t num_tokens,
+                         int64_t max_tokens, int64_t hidden, int64_t inter, int32_t num_experts,
+                         int32_t top_k, int32_t renorm, int32_t ep_size, int32_t ep_rank,
+                         const void* w_gate_up, const void* w_down, void* my_landing,
+                         const uint64_t* peer_landing, uint64_t epoch, void* out,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
 /*
  * Profiling hook: CUDA events (cudaEvent_t handles owned by the caller) that the following
  * calls on this thread record on their stream at stage boundaries — slot 0 route begin,

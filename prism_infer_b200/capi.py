@@ -42,6 +42,16 @@ _SIGNATURES = {
     "prism_moe_block_forward": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _i64, _i64, _i64, _i32,
                                                _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
                                                _vp]),
+    "prism_moe_ep_landing_bytes": (_sz, [_i32, _i64, _i32, _i64, _i32, ctypes.c_int]),
+    "prism_moe_ep_alloc_landing": (ctypes.c_int, [_sz, ctypes.POINTER(_vp), _vp]),
+    "prism_moe_ep_free_landing": (ctypes.c_int, [_vp]),
+    "prism_moe_ep_ipc_handle_bytes": (ctypes.c_int, []),
+    "prism_moe_ep_open_peer": (ctypes.c_int, [_vp, ctypes.POINTER(_vp)]),
+    "prism_moe_ep_close_peer": (ctypes.c_int, [_vp]),
+    "prism_moe_ep_workspace_size": (_sz, [_i64, _i64, _i64, _i32, _i32, _i32, ctypes.c_int]),
+    "prism_moe_ep_forward": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, _i64, _i64, _i64,
+                                            _i64, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp,
+                                            _vp, ctypes.c_uint64, _vp, _vp, _sz, _vp]),
     "prism_moe_profile_events": (ctypes.c_int, [ctypes.POINTER(_vp), _i32]),
     "prism_moe_read_device_error": (ctypes.c_int, [_vp, _vp]),
 }
@@ -211,6 +221,25 @@ def combine(expert_out, topk_weights, entry_row=None, out=None):
                                    ptr(topk_weights), T, k, H, ptr(out),
                                    stream_of(expert_out.device)), "prism_moe_combine")
     return out
+
+
+def ep_alloc_landing(nbytes: int):
+    """Allocate this rank's landing zone; returns (device address, IPC handle bytes)."""
+    lib = load()
+    buf = ctypes.create_string_buffer(lib.prism_moe_ep_ipc_handle_bytes())
+    p = _vp()
+    check(lib.prism_moe_ep_alloc_landing(nbytes, ctypes.byref(p), buf),
+          "prism_moe_ep_alloc_landing")
+    return p.value, buf.raw
+
+
+def ep_open_peer(handle: bytes) -> int:
+    """Map a peer's landing zone from its IPC handle; returns the device address."""
+    lib = load()
+    p = _vp()
+    check(lib.prism_moe_ep_open_peer(ctypes.create_string_buffer(handle, len(handle)),
+                                     ctypes.byref(p)), "prism_moe_ep_open_peer")
+    return p.value
 
 
 def set_profile_events(events) -> None:

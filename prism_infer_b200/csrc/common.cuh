@@ -79,6 +79,16 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// System-scope release store / acquire load (flags shared with peer GPUs over NVLink).
+__device__ __forceinline__ void store_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t load_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Device error word: the first failing kernel records its code; the host reads it.
 __device__ __forceinline__ void record_device_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);

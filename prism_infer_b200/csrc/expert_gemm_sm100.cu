@@ -18,6 +18,7 @@
 
 #include <mutex>
 
+#include "internal.h"
 #include "segments.cuh"
 
 namespace prism {
@@ -35,8 +36,11 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint64_t kWaitNs = 2000000000ull;    // 2 s: far above any legitimate wait
 constexpr uint64_t kDrainNs = 100000000ull;    // 100 ms
 constexpr uint32_t kIdesc = idesc_bf16_f32(kBM, kBN);
-constexpr size_t kSmemBytes =
-    1024 + static_cast<size_t>(kStages) * kStageBytes + 256 + (kMaxSegments + 1) * 4;
+constexpr int kStageRowBytes = 64 * 2 + 16;   // epilogue staging: 64 bf16 + 16 B pad per row
+constexpr size_t kPrefixBytes = ((kMaxSegments + 1) * 4 + 15) / 16 * 16;
+constexpr size_t kStageOutOffset = static_cast<size_t>(kStages) * kStageBytes + 256 + kPrefixBytes;
+constexpr size_t kSmemBytes = 1024 + kStageOutOffset + 4 * 32 * kStageRowBytes;
+static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 enum : int { kGateUp = 0, kDown = 1 };
 
@@ -49,7 +53,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                               const int32_t* __restrict__ seg_offsets,
                               const int32_t* __restrict__ seg_expert, int nseg, int num_kb,
                               int num_n_tiles, int64_t n_out, uint16_t* __restrict__ out,
-                              int64_t out_ld, int32_t rows_cap, int* __restrict__ err) {
+                              int64_t out_ld, int32_t rows_cap, int* __restrict__ err,
+                              GemmOutput tgt) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -190,6 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
     const int row_in_tile = q * 32 + lane;
+    uint8_t* stage_out = smem + kStageOutOffset + (warp - 2) * 32 * kStageRowBytes;
     int it = 0;
     for (int64_t tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++it) {
       const int buf = it & 1;
@@ -207,55 +213,59 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * kBN;
-      const bool valid = row_in_tile < rows_valid;
-      uint16_t* orow = out + static_cast<int64_t>(row0 + row_in_tile) * out_ld;
-      if constexpr (kMode == kGateUp) {
+      // this lane's output row address (0 = no row): dense, or per-row (e.g. a peer GPU)
+      uint64_t my_ptr = 0;
+      if (row_in_tile < rows_valid)
+        my_ptr = tgt.row_ptr ? tgt.row_ptr[row0 + row_in_tile]
+                             : reinterpret_cast<uint64_t>(
+                                   out + static_cast<int64_t>(row0 + row_in_tile) * out_ld);
+      // Each pass stages 32 rows x 64 columns in shared memory, then the warp writes 128-byte
+      // row segments (8 lanes per row, 4 rows per instruction) — full NVLink / DRAM bursts
+      // instead of 32 scattered 16-byte pieces.
+      constexpr int kPassCols = 64;
+      constexpr int kOutCols = kMode == kGateUp ? 128 : kBN;
 #pragma unroll 1
-        for (int c = 0; c < 128; c += 16) {
+      for (int cc = 0; cc < kOutCols; cc += kPassCols) {
+#pragma unroll 1
+        for (int c = 0; c < kPassCols; c += 16) {
           __syncwarp();
-          uint32_t g[16], u[16];
-          tmem_ld16(taddr + c, g);
-          tmem_ld16(taddr + 128 + c, u);
-          tmem_wait_ld();
-          const int64_t col0 = static_cast<int64_t>(nt) * 128 + c;
           uint32_t packed[8];
+          if constexpr (kMode == kGateUp) {
+            uint32_t g[16], u[16];
+            tmem_ld16(taddr + cc + c, g);
+            tmem_ld16(taddr + 128 + cc + c, u);
+            tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float g0 = round_bf16(__uint_as_float(g[2 * i]));
-            const float g1 = round_bf16(__uint_as_float(g[2 * i + 1]));
-            const float u0 = round_bf16(__uint_as_float(u[2 * i]));
-            const float u1 = round_bf16(__uint_as_float(u[2 * i + 1]));
-            packed[i] = pack_bf16x2(silu_f(g0) * u0, silu_f(g1) * u1);
+            for (int i = 0; i < 8; ++i) {
+              const float g0 = round_bf16(__uint_as_float(g[2 * i]));
+              const float g1 = round_bf16(__uint_as_float(g[2 * i + 1]));
+              const float u0 = round_bf16(__uint_as_float(u[2 * i]));
+              const float u1 = round_bf16(__uint_as_float(u[2 * i + 1]));
+              packed[i] = pack_bf16x2(silu_f(g0) * u0, silu_f(g1) * u1);
+            }
+          } else {
+            uint32_t v[16];
+            tmem_ld16(taddr + cc + c, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              packed[i] = pack_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
           }
-          if (valid) {
-            if (col0 + 8 <= n_out)
-              *reinterpret_cast<uint4*>(orow + col0) =
-                  make_uint4(packed[0], packed[1], packed[2], packed[3]);
-            if (col0 + 16 <= n_out)
-              *reinterpret_cast<uint4*>(orow + col0 + 8) =
-                  make_uint4(packed[4], packed[5], packed[6], packed[7]);
-          }
+          uint4* srow = reinterpret_cast<uint4*>(stage_out + lane * kStageRowBytes + c * 2);
+          srow[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+          srow[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
         }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < kBN; c += 16) {
-          __syncwarp();
-          uint32_t v[16];
-          tmem_ld16(taddr + c, v);
-          tmem_wait_ld();
-          const int64_t col0 = static_cast<int64_t>(nt) * kBN + c;
-          uint32_t packed[8];
+        __syncwarp();
+        const int64_t col_base = static_cast<int64_t>(nt) * kOutCols + cc;
+        const int seg = lane & 7;
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            packed[i] = pack_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
-          if (valid) {
-            if (col0 + 8 <= n_out)
-              *reinterpret_cast<uint4*>(orow + col0) =
-                  make_uint4(packed[0], packed[1], packed[2], packed[3]);
-            if (col0 + 16 <= n_out)
-              *reinterpret_cast<uint4*>(orow + col0 + 8) =
-                  make_uint4(packed[4], packed[5], packed[6], packed[7]);
-          }
+        for (int j = 0; j < 8; ++j) {
+          const int r = (lane >> 3) + 4 * j;
+          const uint64_t p = __shfl_sync(0xffffffffu, my_ptr, r);
+          const int64_t col = col_base + seg * 8;
+          if (p != 0 && col + 8 <= n_out)
+            *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p) + col) =
+                *reinterpret_cast<const uint4*>(stage_out + r * kStageRowBytes + seg * 16);
         }
       }
       tc_fence_before();
@@ -263,12 +273,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  if (tgt.done_counter != nullptr && warp >= 2) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
+  }
+  // completion signal: the last CTA to get here publishes `epoch` to every flag
+  if (tgt.done_counter != nullptr && threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned int prev = atomicAdd(tgt.done_counter, 1u);
+    if (prev == gridDim.x - 1) {
+      *tgt.done_counter = 0u;  // ready for the next launch (stream-ordered)
+      __threadfence_system();
+      for (int i = 0; i < tgt.num_signal; ++i) store_release_sys(tgt.signal_flags[i], tgt.epoch);
+    }
   }
 }
 
@@ -317,7 +338,7 @@ int encode_bf16_map(CUtensorMap* map, const void* base, int rank, const uint64_t
 template <int kMode>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const int32_t* seg_offsets,
                 const int32_t* seg_expert, int nseg, int64_t rows_cap, int64_t K, int64_t n_out,
-                uint16_t* out, int* err, cudaStream_t st) {
+                uint16_t* out, int* err, const GemmOutput& tgt, cudaStream_t st) {
   static std::once_flag once;
   static cudaError_t attr_status = cudaSuccess;
   std::call_once(once, [] {
@@ -333,7 +354,7 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const int32_t* seg
   const int grid = static_cast<int>(std::min<int64_t>(num_sms(), std::max<int64_t>(max_tiles, 1)));
   grouped_gemm_sm100_kernel<kMode><<<grid, kThreads, kSmemBytes, st>>>(
       ma, mb, seg_offsets, seg_expert, nseg, num_kb, num_n_tiles, n_out, out, n_out,
-      static_cast<int32_t>(rows_cap), err);
+      static_cast<int32_t>(rows_cap), err, tgt);
   PRISM_LAUNCH_CHECK("grouped_gemm_sm100_kernel launch");
   return PRISM_MOE_OK;
 }
@@ -343,7 +364,9 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const int32_t* seg
 int expert_swiglu_bf16(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
                        const int32_t* seg_offsets, const int32_t* seg_expert, int nseg, int El,
                        const void* wgu, const void* wd, void* y, void* h, int* err,
-                       cudaStream_t st) {
+                       cudaStream_t st, const GemmOutput* down_out) {
+  const GemmOutput dense{};
+  const GemmOutput& down_tgt = down_out ? *down_out : dense;
   PRISM_CHECK_ARG(H % 8 == 0 && I % 8 == 0, "bf16 experts need hidden %% 8 == 0 and inter %% 8 == 0");
   PRISM_CHECK_ARG(nseg >= 1 && nseg <= kMaxSegments, "segments %d outside [1, %d]", nseg,
                   kMaxSegments);
@@ -387,11 +410,11 @@ int expert_swiglu_bf16(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
   }
   record_stage(3, st);
   int r = launch_gemm<kGateUp>(a1, b1, seg_offsets, seg_expert, nseg, rows_cap, H, I,
-                               static_cast<uint16_t*>(h), err, st);
+                               static_cast<uint16_t*>(h), err, dense, st);
   if (r) return r;
   record_stage(4, st);
   r = launch_gemm<kDown>(a2, b2, seg_offsets, seg_expert, nseg, rows_cap, I, H,
-                         static_cast<uint16_t*>(y), err, st);
+                         static_cast<uint16_t*>(y), err, down_tgt, st);
   record_stage(5, st);
   return r;
 }

@@ -8,6 +8,18 @@
 
 namespace prism {
 
+// Where a grouped GEMM writes its output rows and how it announces completion. Default: dense
+// rows ``out + r * ld``. With ``row_ptr``, row r goes to the address row_ptr[r] (any GPU's
+// memory reachable by peer access). With ``done_counter``, the last CTA to finish fences at
+// system scope and stores ``epoch`` to each of the ``num_signal`` flag addresses.
+struct GemmOutput {
+  const uint64_t* row_ptr = nullptr;
+  uint64_t* const* signal_flags = nullptr;
+  int num_signal = 0;
+  uint64_t epoch = 0;
+  unsigned int* done_counter = nullptr;
+};
+
 // route.cu
 int route_topk(const void* logits, int dtype, int64_t T, int E, int k, int renorm, int64_t* ids,
                void* w, int32_t* counts, cudaStream_t st);
@@ -20,11 +32,12 @@ int build_plan(const int64_t* ids, int64_t T, int k, int E, int W, int64_t* perm
 int permute_rows(const void* x, int64_t T, int64_t row_bytes, int k, const int32_t* entry_row,
                  void* xs, cudaStream_t st);
 
-// expert_gemm_sm100.cu — records profiling stage slots 3, 4, 5
+// expert_gemm_sm100.cu — records profiling stage slots 3, 4, 5. ``down_out`` (optional)
+// redirects the down GEMM's rows (y may then be NULL) and adds a completion signal.
 int expert_swiglu_bf16(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
                        const int32_t* seg_offsets, const int32_t* seg_expert, int nseg, int El,
                        const void* wgu, const void* wd, void* y, void* h, int* err,
-                       cudaStream_t st);
+                       cudaStream_t st, const GemmOutput* down_out = nullptr);
 
 // expert_gemm_simt.cu
 int expert_swiglu_f32(const float* x, int64_t rows_cap, int64_t H, int64_t I,

@@ -69,7 +69,7 @@ class ExpertParallelMoE(ExpertBank):
     _expert_list_name = "local_experts"
 
     def __init__(self, hidden_size: int, intermediate_size: int, num_experts: int,
-                 ep_size: int, ep_rank: int, group=None):
+                 ep_size: int, ep_rank: int, group=None, transport: str | None = None):
         super().__init__()
         assert num_experts % ep_size == 0, "num_experts must be divisible by ep_size"
         self.hidden_size = hidden_size
@@ -80,7 +80,104 @@ class ExpertParallelMoE(ExpertBank):
         self.num_local_experts = num_experts // ep_size
         self.local_expert_base = ep_rank * self.num_local_experts
         self.group = group
+        # "p2p": rows written straight into the owners' memory over NVLink (CUDA IPC mappings,
+        # device-side counts exchange, no host synchronisation); "nccl": all_to_all_single with
+        # a host read of the split sizes, like the reference. None picks p2p for bf16 on CUDA.
+        self.transport = transport
+        self._p2p = None
+        self._epoch = 0
         self._init_bank(self.num_local_experts, hidden_size, intermediate_size)
+
+    # ------------------------------------------------------------------ NVLink peer transport
+
+    def use_p2p(self, x: torch.Tensor) -> bool:
+        if self.transport == "nccl" or _KERNELS is not capi:
+            return False
+        if self.transport == "p2p":
+            return True
+        return x.is_cuda and x.dtype == torch.bfloat16 and (
+            self.ep_size == 1 or dist.get_backend(self.group) == "nccl")
+
+    def reserve(self, max_tokens: int, top_k: int) -> None:
+        """Collective: allocate this rank's landing zone for up to ``max_tokens`` tokens per rank
+        (the maximum over ranks is used) and map every peer's. Called by the first forward."""
+        W, me = self.ep_size, self.ep_rank
+        dev = self.w_gate_up.device
+        cap = torch.tensor([max_tokens], dtype=torch.int64, device=dev)
+        if W > 1:
+            dist.all_reduce(cap, op=dist.ReduceOp.MAX, group=self.group)
+        max_tokens = max(256, -(-int(cap.item()) // 256) * 256)
+        lib = capi.load()
+        H, I, E = self.hidden_size, self.intermediate_size, self.num_experts
+        nbytes = lib.prism_moe_ep_landing_bytes(W, max_tokens, top_k, H, E, capi.BF16)
+        ws_bytes = lib.prism_moe_ep_workspace_size(max_tokens, H, I, E, top_k, W, capi.BF16)
+        if nbytes == 0 or ws_bytes == 0:
+            raise RuntimeError("expert-parallel landing zone: invalid shape")
+        self.release()
+        ptr, handle = capi.ep_alloc_landing(nbytes)
+        handles = [None] * W
+        if W > 1:
+            dist.all_gather_object(handles, handle, group=self.group)
+        else:
+            handles[0] = handle
+        peers = [ptr if d == me else capi.ep_open_peer(handles[d]) for d in range(W)]
+        self._p2p = dict(max_tokens=max_tokens, top_k=top_k, ptr=ptr, peers=peers,
+                         table=torch.tensor(peers, dtype=torch.int64, device=dev),
+                         ws=torch.zeros(ws_bytes, dtype=torch.uint8, device=dev))
+        self._epoch = 0
+        if W > 1:
+            dist.barrier(group=self.group)
+
+    def release(self) -> None:
+        """Unmap peers and free the landing zone (collective when W > 1)."""
+        st = self._p2p
+        if st is None:
+            return
+        torch.cuda.synchronize()
+        if self.ep_size > 1 and dist.is_initialized():
+            dist.barrier(group=self.group)
+        lib = capi.load()
+        for d, p in enumerate(st["peers"]):
+            if d != self.ep_rank:
+                lib.prism_moe_ep_close_peer(p)
+        lib.prism_moe_ep_free_landing(st["ptr"])
+        self._p2p = None
+
+    def forward_p2p(self, x: torch.Tensor, router_logits=None, topk_ids=None, topk_weights=None,
+                    top_k: int | None = None, renorm: bool = True) -> torch.Tensor:
+        """One step over NVLink peer memory: route (from logits, or given ids/weights), dispatch
+        into the owners' landing zones, grouped experts, outputs stored back into the sources'
+        landing zones by the down GEMM, combine. Collective over the EP group."""
+        T = x.shape[0]
+        k = top_k if top_k is not None else topk_ids.shape[1]
+        if self._p2p is None or self._p2p["top_k"] != k:
+            self.reserve(T, k)
+        st = self._p2p
+        if T > st["max_tokens"]:
+            raise RuntimeError(f"{T} tokens exceed the expert-parallel landing capacity "
+                               f"{st['max_tokens']}; call reserve() with a larger max_tokens")
+        self._epoch += 1
+        x = x.contiguous()
+        out = torch.empty_like(x)
+        ids = None if topk_ids is None else topk_ids.contiguous()
+        w = None if topk_weights is None else topk_weights.to(x.dtype).contiguous()
+        lg = None if router_logits is None else router_logits.contiguous()
+        lib = capi.load()
+        capi.check(lib.prism_moe_ep_forward(
+            x.data_ptr(), capi.ptr(lg), capi.ptr(ids), capi.ptr(w), capi.BF16, T,
+            st["max_tokens"], self.hidden_size, self.intermediate_size, self.num_experts, k,
+            int(bool(renorm)), self.ep_size, self.ep_rank, self.w_gate_up.data_ptr(),
+            self.w_down.data_ptr(), st["ptr"], st["table"].data_ptr(), self._epoch,
+            out.data_ptr(), st["ws"].data_ptr(), st["ws"].numel(), capi.stream_of(x.device)),
+            "prism_moe_ep_forward")
+        return out
+
+    def check_device_error(self) -> None:
+        """Synchronise and raise if a kernel of the last step recorded an error (a peer wait
+        that ran out shows up here as PRISM_MOE_ERR_TIMEOUT)."""
+        if self._p2p is not None:
+            ws = self._p2p["ws"]
+            capi.check(capi.read_device_error(ws[:4].view(torch.int32)), "expert-parallel step")
 
     def exchange_plan(self, expert_counts: torch.Tensor):
         """Counts exchange (expert_parallel.py:113-127), per local expert instead of per rank:
@@ -108,6 +205,8 @@ class ExpertParallelMoE(ExpertBank):
                 topk_weights: torch.Tensor) -> torch.Tensor:
         """x [T, H], topk_ids [T, k] global expert ids, topk_weights [T, k] -> [T, H]
         (expert_parallel.py:140-176)."""
+        if self.use_p2p(x):
+            return self.forward_p2p(x, topk_ids=topk_ids, topk_weights=topk_weights)
         K = _KERNELS
         T, k = topk_ids.shape
         W, El = self.ep_size, self.num_local_experts

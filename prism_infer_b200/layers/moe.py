@@ -112,6 +112,10 @@ class MoE(ExpertBank):
                                f"{self.gate.weight.dtype}")
         logits = self.gate(x)                     # moe.py:74 — cuBLAS, as in the reference
         if self.ep_size > 1:
+            if self.ep_moe.use_p2p(x):
+                out = self.ep_moe.forward_p2p(x, router_logits=logits, top_k=self.top_k,
+                                              renorm=self.norm_topk_prob)
+                return out.view(orig_shape)
             ids, w, _ = capi.route_topk(logits, self.top_k, self.norm_topk_prob)
             return self.ep_moe(x, ids, w).view(orig_shape)
         out = torch.empty_like(x)

@@ -20,7 +20,7 @@ REPO = Path(__file__).resolve().parent.parent
 BF16_MAX_ABS, BF16_MEAN_REL = 2e-2, 1e-2
 
 
-def _worker(rank, W, port, case, outdir):
+def _worker(rank, W, port, case, outdir, transport):
     sys.path.insert(0, str(REPO))
     from datetime import timedelta
 
@@ -45,13 +45,18 @@ def _worker(rank, W, port, case, outdir):
         moe.ep_moe.w_gate_up.copy_(torch.from_numpy(wts.w_gate_up[rank * El:(rank + 1) * El]))
         moe.ep_moe.w_down.copy_(torch.from_numpy(wts.w_down[rank * El:(rank + 1) * El]))
     moe = moe.to(dev, torch.bfloat16)
+    moe.ep_moe.transport = transport
     x = synthetic.make_hidden_np(Ts[rank], H, seed + 100 * (rank + 1))
     xt = torch.from_numpy(x).to(dev, torch.bfloat16)
     with torch.inference_mode():
         logits, ids, _ = moe.route(xt)
         out = moe(xt)
-        out2 = moe(xt)              # a second call reuses every buffer
+        out2 = moe(xt)              # second and third calls cycle both buffer parities
+        out3 = moe(xt)
     torch.cuda.synchronize()
+    if transport == "p2p":
+        moe.ep_moe.check_device_error()
+        assert torch.equal(out2, out3)
     np.savez(Path(outdir) / f"r{rank}.npz", x=x, logits=logits.float().cpu().numpy(),
              ids=ids.cpu().numpy(), out=out.float().cpu().numpy(),
              out2=out2.float().cpu().numpy())
@@ -66,9 +71,10 @@ CASES = [
 ]
 
 
+@pytest.mark.parametrize("transport", ["p2p", "nccl"])
 @pytest.mark.parametrize("W", [2, 4])
 @pytest.mark.parametrize("case", CASES, ids=["ragged", "qwen30b", "tiny"])
-def test_ep_matches_oracle(W, case):
+def test_ep_matches_oracle(W, case, transport):
     if torch.cuda.device_count() < W:
         pytest.skip(f"needs {W} GPUs")
     import torch.multiprocessing as mp
@@ -81,7 +87,7 @@ def test_ep_matches_oracle(W, case):
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     with tempfile.TemporaryDirectory() as d:
-        mp.start_processes(_worker, args=(W, port, (H, E, k, I, Ts, seed), d), nprocs=W,
+        mp.start_processes(_worker, args=(W, port, (H, E, k, I, Ts, seed), d, transport), nprocs=W,
                            join=True, start_method="spawn")
         res = [dict(np.load(Path(d) / f"r{r}.npz")) for r in range(W)]
     wts = synthetic.make_weights_np(H, E, I, seed)
