@@ -377,7 +377,9 @@ def run_ours(args):
         perm_bytes = T * H * el + rows * H * el + rows * 4
         comb_bytes = rows * H * el + T * H * el + rows * (4 + el)
         extra["hbm"] = {
-            "permute_gbs": perm_bytes / (stage_ms["permute"] / 1e3) / 1e9,
+            # bf16 fuses the permutation into the gate_up GEMM's gather loads
+            "permute_gbs": (perm_bytes / (stage_ms["permute"] / 1e3) / 1e9
+                            if stage_ms["permute"] > 1e-3 else "fused into gate_up"),
             "combine_gbs": comb_bytes / (stage_ms["combine"] / 1e3) / 1e9,
             "route_gbs": (T * E * el + T * k * (8 + el)) / (stage_ms["route"] / 1e3) / 1e9,
             "peak_gbs": hbm_peak,

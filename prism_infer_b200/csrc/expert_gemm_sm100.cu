@@ -1,21 +1,35 @@
 // Kernel 4 — grouped SwiGLU expert GEMMs on 5th-generation tensor cores (bf16, sm_100a).
 //
 // Two persistent launches over a device-side segment table (rows of one expert per segment):
-//   GATE_UP: per tile, D[128 x 256] = X[128 rows, H] * [Wg(128 rows); Wu(128 rows)]^T — the gate
-//            and up halves of one 128-column slice of the intermediate dimension side by side in
-//            one N=256 MMA; the epilogue computes h = silu(bf16(g)) * bf16(u) and stores bf16.
-//   DOWN:    per tile, D[128 x 256] = H[128 rows, I] * Wd(256 rows)^T, stored as bf16.
+//   GATE_UP: per tile, D[rows x 256] = X[rows, H] * [Wg(128 rows); Wu(128 rows)]^T — the gate and
+//            up halves of one 128-column slice of the intermediate dimension side by side in one
+//            N=256 MMA; the epilogue computes h = silu(bf16(g)) * bf16(u) and stores bf16.
+//   DOWN:    per tile, D[rows x 256] = H[rows, I] * Wd(256 rows)^T, stored as bf16.
+// Two tile engines, same code:
+//   single  (kPair=false): one CTA per tile of 128 rows; MMA M=128, N=256, K=16; stage =
+//           A 16 KB + B 32 KB, 4 stages.
+//   pair    (kPair=true):  a cluster of two CTAs on two SMs per tile of 256 rows; the even CTA
+//           issues tcgen05.mma.cta_group::2 (M=256 across both SMs, N=256): each CTA stages its
+//           own 128 A rows and HALF of B (GATE_UP: gate rows in CTA 0, up rows in CTA 1; DOWN:
+//           output columns 0-127 / 128-255), 32 KB per stage, 6 stages — a third less shared
+//           memory traffic per FLOP than the single engine. Both CTAs' TMA completions count on
+//           the even CTA's barrier; MMA completions are committed to both CTAs' barriers; each CTA
+//           drains its own 128 accumulator rows from its TMEM.
 // Warp roles (192 threads, one CTA per SM):
-//   warp 0      TMA producer (one lane): A and B tiles, 4-stage ring of 48 KB stages;
-//   warp 1      TMEM owner + MMA issuer (one lane): tcgen05.mma kind::f16, M=128 N=256 K=16,
-//               fp32 accumulators in TMEM, two 256-column accumulators (512 columns) so the
-//               epilogue of tile i overlaps the MMAs of tile i+1;
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 16 columns, convert, 16-byte global stores.
-// Operands are K-major with the 128-byte swizzle TMA writes. No multicast anywhere. Every wait
-// is bounded; a wait that runs out records PRISM_MOE_ERR_TIMEOUT and the CTA drains its
-// in-flight copies and MMAs before releasing TMEM.
+//   warp 0      TMA producer (one lane);
+//   warp 1      TMEM owner + MMA issuer (one lane; in a pair only the even CTA issues), fp32
+//               accumulators in TMEM, two 256-column accumulators (512 columns) so the epilogue
+//               of tile i overlaps the MMAs of tile i+1;
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 16 columns, convert, stage 64 columns per row in
+//               shared memory, store 128-byte row segments (dense, or per-row addresses that may
+//               point into a peer GPU's memory).
+// Operands are K-major with the 128-byte swizzle TMA writes; no TMA multicast. Every wait is
+// bounded; a wait that runs out records PRISM_MOE_ERR_TIMEOUT and the CTA drains its in-flight
+// copies and MMAs before releasing TMEM.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "internal.h"
@@ -24,29 +38,54 @@
 namespace prism {
 namespace {
 
-constexpr int kBM = 128;
 constexpr int kBK = 64;   // 64 bf16 = 128 bytes = one swizzle row
 constexpr int kBN = 256;  // MMA N
-constexpr int kStages = 4;
-constexpr int kABytes = kBM * kBK * 2;
-constexpr int kBBytes = kBN * kBK * 2;
-constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kThreads = 192;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint64_t kWaitNs = 2000000000ull;    // 2 s: far above any legitimate wait
 constexpr uint64_t kDrainNs = 100000000ull;    // 100 ms
-constexpr uint32_t kIdesc = idesc_bf16_f32(kBM, kBN);
 constexpr int kStageRowBytes = 64 * 2 + 16;   // epilogue staging: 64 bf16 + 16 B pad per row
 constexpr size_t kPrefixBytes = ((kMaxSegments + 1) * 4 + 15) / 16 * 16;
-constexpr size_t kStageOutOffset = static_cast<size_t>(kStages) * kStageBytes + 256 + kPrefixBytes;
-constexpr size_t kSmemBytes = 1024 + kStageOutOffset + 4 * 32 * kStageRowBytes;
-static_assert(kSmemBytes <= 232448, "shared memory budget");
+
+template <bool kPair>
+struct Cfg {
+  static constexpr int kRows = kPair ? 256 : 128;           // rows per tile
+  static constexpr int kABytes = 128 * kBK * 2;              // this CTA's A rows
+  static constexpr int kBBytes = (kPair ? 128 : 256) * kBK * 2;   // this CTA's B rows
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = kPair ? 6 : 4;
+  static constexpr uint32_t kTxBytes = (kPair ? 2 : 1) * kStageBytes;   // per full barrier
+  static constexpr uint32_t kIdesc = idesc_bf16_f32(kRows, kBN);
+  static constexpr size_t kStageOutOffset =
+      static_cast<size_t>(kStages) * kStageBytes + 256 + kPrefixBytes;
+  static constexpr size_t kSmemBytes = 1024 + kStageOutOffset + 4 * 32 * kStageRowBytes;
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
 
 enum : int { kGateUp = 0, kDown = 1 };
 
-__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
+// Two fp32 values -> packed bf16x2 (round to nearest even) in one instruction; lo in bits 0-15.
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
 
-template <int kMode>
+// SwiGLU of one (gate, up) pair of fp32 accumulators: both rounded to bf16 first (the reference
+// materialises gate_up in bf16), then silu(g) * u = g*u / (1 + e^-g) in fp32 with the fast
+// exponential and reciprocal — the result is rounded to bf16, far coarser than their error.
+__device__ __forceinline__ uint32_t swiglu_pair(uint32_t g0b, uint32_t g1b, uint32_t u0b,
+                                                uint32_t u1b) {
+  const uint32_t gp = cvt_bf16x2(__uint_as_float(g0b), __uint_as_float(g1b));
+  const uint32_t up = cvt_bf16x2(__uint_as_float(u0b), __uint_as_float(u1b));
+  const float g0 = __uint_as_float(gp << 16), g1 = __uint_as_float(gp & 0xffff0000u);
+  const float u0 = __uint_as_float(up << 16), u1 = __uint_as_float(up & 0xffff0000u);
+  const float s0 = __fdividef(g0 * u0, 1.0f + __expf(-g0));
+  const float s1 = __fdividef(g1 * u1, 1.0f + __expf(-g1));
+  return cvt_bf16x2(s0, s1);
+}
+
+template <int kMode, bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
                               const __grid_constant__ CUtensorMap tmap_b,
@@ -55,30 +94,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                               int num_n_tiles, int64_t n_out, uint16_t* __restrict__ out,
                               int64_t out_ld, int32_t rows_cap, int* __restrict__ err,
                               GemmOutput tgt) {
+  using C = Cfg<kPair>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* stages = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
-  uint64_t* empty = full + kStages;
-  uint64_t* acc_full = empty + kStages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* acc_full = empty + C::kStages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int32_t* prefix = reinterpret_cast<int32_t*>(smem + kStages * kStageBytes + 256);
+  int32_t* prefix = reinterpret_cast<int32_t*>(smem + C::kStages * C::kStageBytes + 256);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = kPair ? cluster_ctarank() : 0u;     // position in the CTA pair
+  const bool leader = rank == 0;
+  const int64_t unit = kPair ? blockIdx.x / 2 : blockIdx.x;   // tile-scheduling unit
+  const int64_t num_units = kPair ? gridDim.x / 2 : gridDim.x;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 128);
+      mbar_init(&acc_empty[b], kPair ? 256 : 128);
     }
     mbar_init(drain, 1);
     *abort = 0;
@@ -87,12 +131,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmap_b);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+    if constexpr (kPair) {
+      tmem_alloc_pair(tmem_slot, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
   }
-  if (warp == 2) build_tile_prefix(seg_offsets, nseg, kBM, prefix);
+  if (warp == 2) build_tile_prefix(seg_offsets, nseg, C::kRows, prefix);
   tc_fence_before();
-  __syncthreads();
+  if constexpr (kPair)
+    cluster_sync();   // both CTAs' barriers initialised before any cross-CTA arrival
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int64_t total_tiles = static_cast<int64_t>(prefix[nseg]) * num_n_tiles;
@@ -104,30 +156,40 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t issued = 0;           // bit s: stage s has a load issued
     uint32_t issued_parity = 0;    // bit s: full-barrier parity of that load
     bool ok = true;
-    for (int64_t tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+    for (int64_t tile = unit; ok && tile < total_tiles; tile += num_units) {
       const int32_t mt = static_cast<int32_t>(tile / num_n_tiles);
       const int nt = static_cast<int>(tile % num_n_tiles);
       const int s = find_segment(prefix, nseg, mt);
       const int e = seg_expert ? seg_expert[s] : s;
-      const int32_t row0 = seg_offsets[s] + (mt - prefix[s]) * kBM;
+      const int32_t row0 = seg_offsets[s] + (mt - prefix[s]) * C::kRows + 128 * rank;
       for (int kb = 0; kb < num_kb; ++kb) {
         if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort, kWaitNs)) {
           ok = false;
           break;
         }
-        uint8_t* sa = stages + stage * kStageBytes;
-        uint8_t* sb = sa + kABytes;
-        mbar_arrive_expect_tx(&full[stage], kStageBytes);
-        tma_load_2d(sa, &tmap_a, &full[stage], kb * kBK, row0);
-        if constexpr (kMode == kGateUp) {
-          tma_load_4d(sb, &tmap_b, &full[stage], kb * kBK, nt * 128, 0, e);
-          tma_load_4d(sb + kBBytes / 2, &tmap_b, &full[stage], kb * kBK, nt * 128, 1, e);
+        uint8_t* sa = stages + stage * C::kStageBytes;
+        uint8_t* sb = sa + C::kABytes;
+        if (leader) mbar_arrive_expect_tx(&full[stage], C::kTxBytes);
+        if constexpr (kPair) {
+          tma_load_2d_pair(sa, &tmap_a, &full[stage], kb * kBK, row0);
+          if constexpr (kMode == kGateUp)
+            tma_load_4d_pair(sb, &tmap_b, &full[stage], kb * kBK, nt * 128,
+                             static_cast<int32_t>(rank), e);
+          else
+            tma_load_3d_pair(sb, &tmap_b, &full[stage], kb * kBK,
+                             nt * kBN + 128 * static_cast<int32_t>(rank), e);
         } else {
-          tma_load_3d(sb, &tmap_b, &full[stage], kb * kBK, nt * kBN, e);
+          tma_load_2d(sa, &tmap_a, &full[stage], kb * kBK, row0);
+          if constexpr (kMode == kGateUp) {
+            tma_load_4d(sb, &tmap_b, &full[stage], kb * kBK, nt * 128, 0, e);
+            tma_load_4d(sb + C::kBBytes / 2, &tmap_b, &full[stage], kb * kBK, nt * 128, 1, e);
+          } else {
+            tma_load_3d(sb, &tmap_b, &full[stage], kb * kBK, nt * kBN, e);
+          }
         }
         issued |= 1u << stage;
         issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-        if (++stage == kStages) {
+        if (++stage == C::kStages) {
           stage = 0;
           phase ^= 1;
         }
@@ -137,21 +199,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       *abort = 1;
       record_device_error(err, PRISM_MOE_ERR_TIMEOUT);
     }
-    if (*abort) {
-      // let every copy this thread issued land before the CTA can exit
-      for (int s = 0; s < kStages; ++s)
+    if (*abort && leader) {
+      // let every copy of the pair land before either CTA can exit (the even CTA's full
+      // barriers count both CTAs' bytes)
+      for (int s = 0; s < C::kStages; ++s)
         if ((issued >> s) & 1u) {
           volatile int never = 0;
           mbar_wait_bounded(&full[s], (issued_parity >> s) & 1u, &never, kDrainNs);
         }
     }
-  } else if (warp == 1 && lane == 0) {
+  } else if (warp == 1 && lane == 0 && leader) {
     // ------------------------------------------------------------------ MMA issuer
     int stage = 0;
     uint32_t phase = 0;
     int it = 0;
     bool ok = true;
-    for (int64_t tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, ++it) {
+    for (int64_t tile = unit; ok && tile < total_tiles; tile += num_units, ++it) {
       const int buf = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait_bounded(&acc_empty[buf], acc_phase ^ 1, abort, kWaitNs)) {
@@ -166,44 +229,59 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t a0 = smem_u32(stages + stage * kStageBytes);
-        const uint32_t b0 = a0 + kABytes;
+        const uint32_t a0 = smem_u32(stages + stage * C::kStageBytes);
+        const uint32_t b0 = a0 + C::kABytes;
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk) {
-          tc_mma_bf16(d_tmem, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32),
-                      kIdesc, (kb | kk) != 0 ? 1u : 0u);
+          const uint64_t ad = smem_desc_sw128(a0 + kk * 32), bd = smem_desc_sw128(b0 + kk * 32);
+          const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
+          if constexpr (kPair)
+            tc_mma_bf16_pair(d_tmem, ad, bd, C::kIdesc, acc);
+          else
+            tc_mma_bf16(d_tmem, ad, bd, C::kIdesc, acc);
         }
-        tc_commit(&empty[stage]);
-        if (++stage == kStages) {
+        if constexpr (kPair)
+          tc_commit_pair(&empty[stage], 0x3);
+        else
+          tc_commit(&empty[stage]);
+        if (++stage == C::kStages) {
           stage = 0;
           phase ^= 1;
         }
       }
       if (!ok) break;
-      tc_commit(&acc_full[buf]);
+      if constexpr (kPair)
+        tc_commit_pair(&acc_full[buf], 0x3);
+      else
+        tc_commit(&acc_full[buf]);
     }
     if (!ok) {
       *abort = 1;
       record_device_error(err, PRISM_MOE_ERR_TIMEOUT);
     }
     if (*abort) {
-      tc_commit(drain);   // completes once every MMA issued above has finished
+      if constexpr (kPair)
+        tc_commit_pair(drain, 0x1);
+      else
+        tc_commit(drain);   // completes once every MMA issued above has finished
       volatile int never = 0;
       mbar_wait_bounded(drain, 0, &never, kDrainNs);
     }
   } else if (warp >= 2) {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
-    const int row_in_tile = q * 32 + lane;
-    uint8_t* stage_out = smem + kStageOutOffset + (warp - 2) * 32 * kStageRowBytes;
+    const int row_in_tile = q * 32 + lane;  // row within this CTA's 128 rows
+    uint8_t* stage_out = smem + C::kStageOutOffset + (warp - 2) * 32 * kStageRowBytes;
+    const uint32_t acc_empty_leader =
+        kPair ? mapa_shared(smem_u32(&acc_empty[0]), 0) : smem_u32(&acc_empty[0]);
     int it = 0;
-    for (int64_t tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++it) {
+    for (int64_t tile = unit; tile < total_tiles; tile += num_units, ++it) {
       const int buf = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       const int32_t mt = static_cast<int32_t>(tile / num_n_tiles);
       const int nt = static_cast<int>(tile % num_n_tiles);
       const int s = find_segment(prefix, nseg, mt);
-      const int32_t row0 = seg_offsets[s] + (mt - prefix[s]) * kBM;
+      const int32_t row0 = seg_offsets[s] + (mt - prefix[s]) * C::kRows + 128 * rank;
       const int32_t seg_end = seg_offsets[s + 1];
       const int32_t rows_valid = (seg_end < rows_cap ? seg_end : rows_cap) - row0;
       if (!mbar_wait_bounded(&acc_full[buf], acc_phase, abort, kWaitNs)) {
@@ -227,33 +305,33 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (int cc = 0; cc < kOutCols; cc += kPassCols) {
 #pragma unroll 1
-        for (int c = 0; c < kPassCols; c += 16) {
+        for (int c = 0; c < kPassCols; c += 32) {   // 32 columns per tcgen05.wait::ld
           __syncwarp();
-          uint32_t packed[8];
+          uint32_t packed[16];
           if constexpr (kMode == kGateUp) {
-            uint32_t g[16], u[16];
-            tmem_ld16(taddr + cc + c, g);
-            tmem_ld16(taddr + 128 + cc + c, u);
+            uint32_t g[32], u[32];
+            tmem_ld16(taddr + cc + c, *reinterpret_cast<uint32_t(*)[16]>(&g[0]));
+            tmem_ld16(taddr + cc + c + 16, *reinterpret_cast<uint32_t(*)[16]>(&g[16]));
+            tmem_ld16(taddr + 128 + cc + c, *reinterpret_cast<uint32_t(*)[16]>(&u[0]));
+            tmem_ld16(taddr + 128 + cc + c + 16, *reinterpret_cast<uint32_t(*)[16]>(&u[16]));
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float g0 = round_bf16(__uint_as_float(g[2 * i]));
-              const float g1 = round_bf16(__uint_as_float(g[2 * i + 1]));
-              const float u0 = round_bf16(__uint_as_float(u[2 * i]));
-              const float u1 = round_bf16(__uint_as_float(u[2 * i + 1]));
-              packed[i] = pack_bf16x2(silu_f(g0) * u0, silu_f(g1) * u1);
-            }
+            for (int i = 0; i < 16; ++i)
+              packed[i] = swiglu_pair(g[2 * i], g[2 * i + 1], u[2 * i], u[2 * i + 1]);
           } else {
-            uint32_t v[16];
-            tmem_ld16(taddr + cc + c, v);
+            uint32_t v[32];
+            tmem_ld16(taddr + cc + c, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+            tmem_ld16(taddr + cc + c + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              packed[i] = pack_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+            for (int i = 0; i < 16; ++i)
+              packed[i] = cvt_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
           }
           uint4* srow = reinterpret_cast<uint4*>(stage_out + lane * kStageRowBytes + c * 2);
-          srow[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-          srow[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4)
+            srow[q4] = make_uint4(packed[4 * q4], packed[4 * q4 + 1], packed[4 * q4 + 2],
+                                  packed[4 * q4 + 3]);
         }
         __syncwarp();
         const int64_t col_base = static_cast<int64_t>(nt) * kOutCols + cc;
@@ -269,17 +347,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&acc_empty[buf]);
+      if constexpr (kPair)
+        mbar_arrive_cluster(acc_empty_leader + buf * 8);
+      else
+        mbar_arrive(&acc_empty[buf]);
     }
   }
 
   if (tgt.done_counter != nullptr && warp >= 2) __threadfence_system();
   tc_fence_before();
-  __syncthreads();
+  if constexpr (kPair)
+    cluster_sync();   // neither CTA leaves while its partner may still use its TMEM / smem
+  else
+    __syncthreads();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    if constexpr (kPair)
+      tmem_dealloc_pair(tmem_base, kTmemCols);
+    else
+      tmem_dealloc(tmem_base, kTmemCols);
   }
   // completion signal: the last CTA to get here publishes `epoch` to every flag
   if (tgt.done_counter != nullptr && threadIdx.x == 0) {
@@ -335,28 +422,73 @@ int encode_bf16_map(CUtensorMap* map, const void* base, int rank, const uint64_t
   return PRISM_MOE_OK;
 }
 
-template <int kMode>
+template <int kMode, bool kPair>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const int32_t* seg_offsets,
                 const int32_t* seg_expert, int nseg, int64_t rows_cap, int64_t K, int64_t n_out,
                 uint16_t* out, int* err, const GemmOutput& tgt, cudaStream_t st) {
+  using C = Cfg<kPair>;
+  auto kern = grouped_gemm_sm100_kernel<kMode, kPair>;
   static std::once_flag once;
   static cudaError_t attr_status = cudaSuccess;
-  std::call_once(once, [] {
-    attr_status = cudaFuncSetAttribute(grouped_gemm_sm100_kernel<kMode>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(kSmemBytes));
+  static int max_units = 0;
+  std::call_once(once, [&] {
+    attr_status = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(C::kSmemBytes));
+    max_units = num_sms();
+    if (attr_status == cudaSuccess && kPair) {
+      // how many CTA pairs can be resident at once
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(2 * (num_sms() / 2), 1, 1);
+      cfg.blockDim = dim3(kThreads, 1, 1);
+      cfg.dynamicSmemBytes = C::kSmemBytes;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) == cudaSuccess && clusters > 0)
+        max_units = clusters;
+      else
+        max_units = num_sms() / 2;
+      cudaGetLastError();
+    }
   });
   PRISM_CUDA(attr_status);
   const int n_tile = kMode == kGateUp ? 128 : kBN;
   const int num_n_tiles = static_cast<int>(ceil_div(n_out, n_tile));
   const int num_kb = static_cast<int>(ceil_div(K, kBK));
-  const int64_t max_tiles = (ceil_div(rows_cap, kBM) + nseg) * num_n_tiles;
-  const int grid = static_cast<int>(std::min<int64_t>(num_sms(), std::max<int64_t>(max_tiles, 1)));
-  grouped_gemm_sm100_kernel<kMode><<<grid, kThreads, kSmemBytes, st>>>(
-      ma, mb, seg_offsets, seg_expert, nseg, num_kb, num_n_tiles, n_out, out, n_out,
-      static_cast<int32_t>(rows_cap), err, tgt);
-  PRISM_LAUNCH_CHECK("grouped_gemm_sm100_kernel launch");
+  const int64_t max_tiles = (ceil_div(rows_cap, C::kRows) + nseg) * num_n_tiles;
+  const int units = static_cast<int>(std::min<int64_t>(max_units, std::max<int64_t>(max_tiles, 1)));
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(static_cast<unsigned>(units * (kPair ? 2 : 1)), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = st;
+  if (kPair) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  PRISM_CUDA(cudaLaunchKernelEx(&cfg, kern, ma, mb, seg_offsets, seg_expert, nseg, num_kb,
+                                num_n_tiles, n_out, out, n_out, static_cast<int32_t>(rows_cap),
+                                err, tgt));
   return PRISM_MOE_OK;
+}
+
+// Pair tiles (256 rows) pay off once segments are long: tail tiles waste up to 255 rows per
+// segment, single tiles up to 127. PRISM_MOE_GEMM_ENGINE=single|pair overrides the choice.
+bool use_pair(int64_t rows_cap, int nseg) {
+  const char* force = std::getenv("PRISM_MOE_GEMM_ENGINE");
+  if (force && force[0] == 's') return false;
+  if (force && force[0] == 'p') return true;
+  return rows_cap / std::max(nseg, 1) >= 2048;
 }
 
 }  // namespace
@@ -376,11 +508,12 @@ int expert_swiglu_bf16(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
                    reinterpret_cast<uintptr_t>(h)) % 16 == 0,
                   "bf16 expert operands must be 16-byte aligned");
   if (rows_cap == 0) return PRISM_MOE_OK;
+  const bool pair = use_pair(rows_cap, nseg);
   CUtensorMap a1, b1, a2, b2;
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(H), static_cast<uint64_t>(rows_cap)};
     const uint64_t strides[1] = {static_cast<uint64_t>(H) * 2};
-    const uint32_t box[2] = {kBK, kBM};
+    const uint32_t box[2] = {kBK, 128};
     int r = encode_bf16_map(&a1, xs, 2, dims, strides, box);
     if (r) return r;
   }
@@ -396,7 +529,7 @@ int expert_swiglu_bf16(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(I), static_cast<uint64_t>(rows_cap)};
     const uint64_t strides[1] = {static_cast<uint64_t>(I) * 2};
-    const uint32_t box[2] = {kBK, kBM};
+    const uint32_t box[2] = {kBK, 128};
     int r = encode_bf16_map(&a2, h, 2, dims, strides, box);
     if (r) return r;
   }
@@ -404,17 +537,21 @@ int expert_swiglu_bf16(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
     const uint64_t dims[3] = {static_cast<uint64_t>(I), static_cast<uint64_t>(H),
                               static_cast<uint64_t>(El)};
     const uint64_t strides[2] = {static_cast<uint64_t>(I) * 2, static_cast<uint64_t>(H * I) * 2};
-    const uint32_t box[3] = {kBK, kBN, 1};
+    const uint32_t box[3] = {kBK, static_cast<uint32_t>(pair ? 128 : kBN), 1};
     int r = encode_bf16_map(&b2, wd, 3, dims, strides, box);
     if (r) return r;
   }
   record_stage(3, st);
-  int r = launch_gemm<kGateUp>(a1, b1, seg_offsets, seg_expert, nseg, rows_cap, H, I,
-                               static_cast<uint16_t*>(h), err, dense, st);
+  int r = pair ? launch_gemm<kGateUp, true>(a1, b1, seg_offsets, seg_expert, nseg, rows_cap, H,
+                                            I, static_cast<uint16_t*>(h), err, dense, st)
+               : launch_gemm<kGateUp, false>(a1, b1, seg_offsets, seg_expert, nseg, rows_cap, H,
+                                             I, static_cast<uint16_t*>(h), err, dense, st);
   if (r) return r;
   record_stage(4, st);
-  r = launch_gemm<kDown>(a2, b2, seg_offsets, seg_expert, nseg, rows_cap, I, H,
-                         static_cast<uint16_t*>(y), err, down_tgt, st);
+  r = pair ? launch_gemm<kDown, true>(a2, b2, seg_offsets, seg_expert, nseg, rows_cap, I, H,
+                                      static_cast<uint16_t*>(y), err, down_tgt, st)
+           : launch_gemm<kDown, false>(a2, b2, seg_offsets, seg_expert, nseg, rows_cap, I, H,
+                                       static_cast<uint16_t*>(y), err, down_tgt, st);
   record_stage(5, st);
   return r;
 }

@@ -169,10 +169,15 @@ def _segments(counts, device=DEV):
     (320, 200, [129, 64]),                         # K, N not multiples of the tile
     (4096, 1536, [300]),                           # Qwen3-235B-A22B expert shape
 ])
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-def test_expert_swiglu_matches_oracle(H, I, counts, dtype):
+@pytest.mark.parametrize("dtype,engine", [(torch.bfloat16, "single"), (torch.bfloat16, "pair"),
+                                          (torch.float32, "simt")])
+def test_expert_swiglu_matches_oracle(H, I, counts, dtype, engine, monkeypatch):
+    """``engine``: bf16 tcgen05 single-CTA tiles (128 rows) or CTA-pair tiles (256 rows,
+    cta_group::2); fp32 runs on CUDA cores."""
     if dtype == torch.float32 and H * I > 2048 * 768:
         pytest.skip("fp32 CUDA-core path is exercised at the smaller shapes")
+    if dtype == torch.bfloat16:
+        monkeypatch.setenv("PRISM_MOE_GEMM_ENGINE", engine)
     gen = torch.Generator(device=DEV).manual_seed(H + I + len(counts))
     E = len(counts)
     R = int(sum(counts))
@@ -202,8 +207,10 @@ def test_expert_swiglu_matches_oracle(H, I, counts, dtype):
             np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-5)
 
 
-def test_expert_swiglu_segment_expert_map():
+@pytest.mark.parametrize("engine", ["single", "pair"])
+def test_expert_swiglu_segment_expert_map(engine, monkeypatch):
     """Segments may name any local expert (EP receiver layout: (source rank, local expert))."""
+    monkeypatch.setenv("PRISM_MOE_GEMM_ENGINE", engine)
     H, I, El = 256, 128, 3
     x = torch.randn(300, H, device=DEV).to(torch.bfloat16)
     wgu = (torch.randn(El, 2 * I, H, device=DEV) / 16).to(torch.bfloat16)
