@@ -291,7 +291,10 @@ def run_ours(args):
     moe.check_device_error(device) if world == 1 else None
 
     # per-stage averages (ms) — slots: route, plan, permute, gate_up, down, combine
-    names = ["route", "plan", "permute", "gate_up", "down", "combine"]
+    # EP>1: "permute" is the exchange (counts all-gather, row dispatch over NVLink, wait for all
+    # sources) and "combine" includes waiting for the owners' down GEMMs to return every row
+    names = ["route", "plan", "permute" if world == 1 else "exchange", "gate_up", "down",
+             "combine"]
     stage_ms = {}
     for s, name in enumerate(names):
         vals = []
@@ -300,13 +303,7 @@ def run_ours(args):
                 vals.append(row[s].elapsed_time(row[s + 1]))
             except RuntimeError:
                 pass
-        stage_ms[name] = sum(vals) / len(vals) if vals and world == 1 else None
-    if world > 1:
-        # EP path records only the expert GEMM slots (3..5)
-        g = [row[3].elapsed_time(row[4]) for row in ev]
-        d = [row[4].elapsed_time(row[5]) for row in ev]
-        stage_ms["gate_up"] = sum(g) / len(g)
-        stage_ms["down"] = sum(d) / len(d)
+        stage_ms[name] = sum(vals) / len(vals) if vals else None
 
     value = world * T * steps / (ms / 1e3)
 

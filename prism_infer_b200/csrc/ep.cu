@@ -234,12 +234,16 @@ __global__ void __launch_bounds__(256)
                        const int32_t* __restrict__ expert_offsets,
                        const int32_t* __restrict__ dst_base, int El,
                        const uint64_t* __restrict__ peers, size_t recv_off,
-                       const uint64_t* __restrict__ flag_b, int W, uint64_t epoch,
+                       const uint64_t* __restrict__ flag_b, int W, int me, uint64_t epoch,
                        unsigned int* __restrict__ done) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t q = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; q < N;
-       q += warps) {
+  // Rows are destination-major; start at the next rank's block so that, at any moment, the
+  // ranks write to different peers instead of all to the same one.
+  const int64_t shift = N > 0 ? expert_offsets[((me + 1) % W) * El] : 0;
+  for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; i < N;
+       i += warps) {
+    const int64_t q = (i + shift) % N;
     const int32_t f = row_entry[q];
     const int64_t e = ids[f];
     const int64_t t = f / k;
@@ -362,10 +366,11 @@ __attribute__((visibility("default"))) int prism_moe_ep_forward(
   PRISM_CHECK_ARG(num_tokens >= 0 && num_tokens <= max_tokens,
                   "ep_forward: num_tokens %lld exceeds the landing capacity %lld",
                   static_cast<long long>(num_tokens), static_cast<long long>(max_tokens));
-  PRISM_CHECK_ARG(router_logits || (topk_ids_in && topk_weights_in),
+  PRISM_CHECK_ARG(num_tokens == 0 || router_logits || (topk_ids_in && topk_weights_in),
                   "ep_forward: needs router_logits or topk ids and weights");
   PRISM_CHECK_ARG(epoch > 0, "ep_forward: epoch must be >= 1 and increase every step");
-  PRISM_CHECK_ARG(my_landing && peer_landing && x && out && w_gate_up && w_down,
+  PRISM_CHECK_ARG(my_landing && peer_landing && w_gate_up && w_down &&
+                      (num_tokens == 0 || (x && out)),
                   "ep_forward: null pointer");
   PRISM_CHECK_ARG(hidden % 8 == 0 && inter % 8 == 0, "ep_forward: hidden, inter % 8 != 0");
   const int64_t es = 2;
@@ -393,9 +398,11 @@ __attribute__((visibility("default"))) int prism_moe_ep_forward(
   int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
   int32_t* entry_row = reinterpret_cast<int32_t*>(ws + L.entry_row);
   int32_t* row_entry = reinterpret_cast<int32_t*>(ws + L.row_entry);
+  record_stage(1, st);
   int r = build_plan(ids, T, k, E, 1, nullptr, nullptr, nullptr, counts, offsets, entry_row,
                      row_entry, ws + L.plan, L.plan_bytes, st);
   if (r) return r;
+  record_stage(2, st);   // exchange: counts all-gather, dispatch, wait for every source
   int32_t* seg_offsets = reinterpret_cast<int32_t*>(ws + L.seg_offsets);
   int32_t* dst_base = reinterpret_cast<int32_t*>(ws + L.dst_base);
   int32_t* recv_base = reinterpret_cast<int32_t*>(ws + L.recv_base);
@@ -419,7 +426,7 @@ __attribute__((visibility("default"))) int prism_moe_ep_forward(
       1, std::min<int64_t>(ceil_div(N, 8), static_cast<int64_t>(num_sms()) * 8)));
   ep_dispatch_kernel<<<dgrid, 256, 0, st>>>(
       static_cast<const uint4*>(x), N, k, hidden * es / 16, ids, row_entry, offsets, dst_base,
-      El, peer_landing, recv_off, flag_b, W, epoch, done);
+      El, peer_landing, recv_off, flag_b, W, me, epoch, done);
   PRISM_LAUNCH_CHECK("ep_dispatch_kernel launch");
   ep_wait_kernel<<<1, 64, 0, st>>>(peer_landing, me, LL.flags, W, 1, epoch, err);
   PRISM_LAUNCH_CHECK("ep_wait_kernel launch");
