@@ -88,6 +88,16 @@ __device__ __forceinline__ uint64_t load_acquire_sys(const uint64_t* p) {
   asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ uint32_t load_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Counter increment that publishes this thread's earlier writes (any GPU's memory) to a thread
+// that reads the counter with load_acquire_sys.
+__device__ __forceinline__ void add_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 // Device error word: the first failing kernel records its code; the host reads it.
 __device__ __forceinline__ void record_device_error(int* err, int code) {

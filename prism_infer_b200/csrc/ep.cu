@@ -5,19 +5,24 @@
 //
 // Every rank owns one "landing zone" (cudaMalloc, mapped by all peers through CUDA IPC) with
 // identical offsets on every rank:
-//   flags   [3 phases][W] u64   phase A counts ready, B rows landed, C outputs landed; slot s is
-//                               written (st.release.sys) by source rank s with the step's epoch
+//   flags   [2 phases][W] u64   phase A counts ready, C outputs landed; slot s is written
+//                               (st.release.sys) by source rank s with the step's epoch
+//   arrive  [2][W*El] u32       per-parity rows landed in each receive segment (red.release.sys
+//                               by the senders' copy warps; reset one step ahead by the owner)
 //   counts  [2][W][E] i32       per-parity all-gathered expert histograms (row = source rank)
-//   recv    [2][W*Tmax*k][H]    rows routed to this rank's experts, expert-major then source
+//   recv    [2][W*Tmax*k][H]    rows routed to this rank's experts, in W*El segments ordered by
+//                               expected arrival (ep_counts_kernel)
 //   back    [2][Tmax*k][H]      this rank's expert outputs, written by the owners' down GEMM
 // Parity = epoch & 1. Double-buffering plus the per-step flag waits make reuse safe: a rank
-// can only reach step i+2's writes into a peer's parity-(i&1) buffers after that peer has
-// finished step i (see the flag chain in the design notes).
+// can only reach step i+2's writes into a peer's parity-(i&1) buffers after it has seen that
+// peer's C flag of step i+1, which the peer raises only after its gate_up GEMM of step i+1 and
+// therefore after it finished reading step i's buffers.
 //
-// Step (prism_moe_ep_forward): route -> plan -> counts all-gather (A) -> return addresses ->
-// dispatch rows straight into the owners' recv buffers (B, last-block signal) -> wait B ->
-// gate_up GEMM -> down GEMM whose epilogue stores every row into its source rank's back
-// buffer and signals C from its last CTA -> wait C -> local weighted combine.
+// Step (prism_moe_ep_forward): route -> plan -> counts all-gather (A) and tables -> gate_up GEMM
+// whose copy warps dispatch the rows into the owners' recv buffers (B, one flag per source,
+// raised when that source's rows to this rank are all written) while its producer waits for
+// the B flag of the source each tile reads -> down GEMM whose epilogue stores every row into
+// its source rank's back buffer and signals C from its last CTA -> wait C -> local combine.
 // Every wait is bounded (kPeerWaitNs); a wait that runs out records PRISM_MOE_ERR_TIMEOUT.
 #include <algorithm>
 #include <cstring>
@@ -30,9 +35,12 @@ namespace {
 
 constexpr uint64_t kPeerWaitNs = 10000000000ull;  // 10 s: peers may start a step late
 constexpr int kMaxRanks = 64;
+constexpr int kMaxExperts = 1024;
+// flags (2 x 64 x 8 B, padded to 4 KB) + arrival counters (2 x 1024 x 4 B); zero at allocation
+constexpr size_t kHeaderBytes = 4096 + 2 * kMaxExperts * sizeof(uint32_t);
 
 struct Landing {
-  size_t flags, counts, recv, back, total;
+  size_t flags, arrive, counts, recv, back, total;
   int64_t rcap;       // rows of one recv parity
   int64_t bcap;       // rows of one back parity
 };
@@ -41,7 +49,8 @@ Landing landing_layout(int W, int64_t max_tokens, int k, int64_t H, int E, int64
   Landing L{};
   size_t o = 0;
   L.flags = o;
-  o += 4096;
+  L.arrive = 4096;
+  o += kHeaderBytes;
   L.counts = o;
   o += align_up(sizeof(int32_t) * 2 * W * E, 256);
   L.rcap = static_cast<int64_t>(W) * max_tokens * k;
@@ -56,13 +65,12 @@ Landing landing_layout(int W, int64_t max_tokens, int k, int64_t H, int E, int64
 
 struct EpWs {
   size_t err, ids, w, plan, plan_bytes, counts, offsets, entry_row, row_entry, seg_offsets,
-      dst_base, recv_base, src_off, flag_b, flag_c, done, row_ptr, h, total;
+      seg_expert, seg_base, dst_base, flag_c, done, h, total;
 };
 
 EpWs ep_ws_layout(int64_t max_tokens, int64_t H, int64_t I, int E, int k, int W, int64_t rcap,
                   int64_t es) {
   EpWs L{};
-  const int El = E / W;
   const int64_t N = max_tokens * k;
   size_t o = 0;
   auto take = [&](size_t bytes) {
@@ -79,14 +87,12 @@ EpWs ep_ws_layout(int64_t max_tokens, int64_t H, int64_t I, int E, int k, int W,
   L.offsets = take(sizeof(int32_t) * (E + 1));
   L.entry_row = take(sizeof(int32_t) * N);
   L.row_entry = take(sizeof(int32_t) * N);
-  L.seg_offsets = take(sizeof(int32_t) * (El + 1));
+  L.seg_offsets = take(sizeof(int32_t) * (E + 1));   // W * El receive segments
+  L.seg_expert = take(sizeof(int32_t) * E);
+  L.seg_base = take(sizeof(uint64_t) * E);
   L.dst_base = take(sizeof(int32_t) * E);
-  L.recv_base = take(sizeof(int32_t) * El * W);
-  L.src_off = take(sizeof(int32_t) * El * W);
-  L.flag_b = take(sizeof(uint64_t) * W);
   L.flag_c = take(sizeof(uint64_t) * W);
   L.done = take(sizeof(unsigned int) * 4);
-  L.row_ptr = take(sizeof(uint64_t) * rcap);
   L.h = take(static_cast<size_t>(es * rcap * I));
   L.total = o;
   return L;
@@ -131,15 +137,23 @@ __device__ int32_t block_excl_scan(int32_t v, int n, int32_t* tmp, int32_t* tota
 }
 
 // Phase A: all-gather the expert histograms, then derive this step's tables.
+//
+// Receive layout on rank d: W * El segments in expected-arrival order. Segment (j, le), index
+// j * El + le, holds the rows of local expert le sent by source (d - j) mod W, in the source's
+// expert-major order. Source s writes to destinations in the order s, s+1, ... (mod W), so the
+// rows it sends to d arrive j = (d - s) mod W slots into its sequence, and d's GEMM reads the
+// segments of the sources that are done first.
 __global__ void __launch_bounds__(1024)
     ep_counts_kernel(const int32_t* __restrict__ my_counts, const uint64_t* __restrict__ peers,
-                     size_t flags_off, size_t counts_off, int W, int me, int E, uint64_t epoch,
-                     int32_t* __restrict__ seg_offsets, int32_t* __restrict__ dst_base,
-                     int32_t* __restrict__ recv_base, int32_t* __restrict__ src_off,
-                     uint64_t* __restrict__ flag_b, uint64_t* __restrict__ flag_c,
+                     size_t flags_off, size_t counts_off, size_t back_off, int64_t row_bytes,
+                     int W, int me, int E, uint64_t epoch, int32_t* __restrict__ seg_offsets,
+                     int32_t* __restrict__ seg_expert, uint64_t* __restrict__ seg_base,
+                     int32_t* __restrict__ dst_base, uint64_t* __restrict__ flag_c,
+                     uint32_t* __restrict__ next_arrive, unsigned int* __restrict__ claim,
                      int* __restrict__ err) {
   __shared__ int32_t tmp[1024];
   __shared__ int32_t total;
+  __shared__ int32_t R[kMaxRanks * kMaxRanks];   // R[d * W + s]: rows source s sends to d
   const int El = E / W;
   const int par = static_cast<int>(epoch & 1);
   // 1. my histogram into row `me` of every rank's counts[par]
@@ -158,120 +172,59 @@ __global__ void __launch_bounds__(1024)
   __threadfence();
   const volatile int32_t* C =
       reinterpret_cast<const volatile int32_t*>(peers[me] + counts_off) + par * W * E;
-  // 3. totals per expert, and offsets of each expert inside its owner's receive layout
-  const int e = threadIdx.x;
-  int32_t tot = 0, before_me = 0;
-  if (e < E)
-    for (int s = 0; s < W; ++s) {
-      const int32_t c = C[s * E + e];
-      tot += c;
-      if (s < me) before_me += c;
-    }
-  const int32_t ex = block_excl_scan(tot, E, tmp, &total);
-  if (e < E) tmp[e] = ex;
-  __syncthreads();
-  if (e < E) {
-    const int32_t within_owner = ex - tmp[(e / El) * El];   // offset inside owner's layout
-    dst_base[e] = within_owner + before_me;
-    if (e / El == me) {
-      const int le = e - me * El;
-      seg_offsets[le] = within_owner;
-      int32_t b = within_owner;
-      for (int s = 0; s < W; ++s) {
-        recv_base[le * W + s] = b;
-        b += C[s * E + e];
-      }
-    }
+  const int i = threadIdx.x;
+  // 3. my receive segments
+  int32_t v = 0;
+  if (i < E) {
+    const int j = i / El, le = i % El;
+    v = C[((me - j + W) % W) * E + me * El + le];
   }
-  __syncthreads();
-  if (e == 0) {
+  const int32_t seg_ex = block_excl_scan(v, E, tmp, &total);
+  if (i < E) {
+    seg_offsets[i] = seg_ex;
+    seg_expert[i] = i % El;
+  }
+  if (i == 0) seg_offsets[E] = total;
+  // 4. rows per (destination, source) pair
+  for (int p = i; p < W * W; p += blockDim.x) {
+    const int d = p / W, s = p % W;
     int32_t r = 0;
-    for (int le = 0; le < El; ++le)
-      for (int s = 0; s < W; ++s) r += C[s * E + me * El + le];
-    seg_offsets[El] = r;
+    for (int le = 0; le < El; ++le) r += C[s * E + d * El + le];
+    R[p] = r;
   }
-  // 4. each source's expert-major row offset of its first row for my expert le
-  for (int s = 0; s < W; ++s) {
-    const int32_t c = e < E ? C[s * E + e] : 0;
-    const int32_t ex_s = block_excl_scan(c, E, tmp, nullptr);
-    if (e < E && e / El == me) src_off[s * El + (e - me * El)] = ex_s;
-  }
-  // 5. where this rank announces B (rows landed) and C (outputs landed) on each peer
-  if (threadIdx.x < W) {
-    flag_b[threadIdx.x] = reinterpret_cast<uint64_t>(flag_addr(peers[threadIdx.x], flags_off, W, 1, me));
-    flag_c[threadIdx.x] = reinterpret_cast<uint64_t>(flag_addr(peers[threadIdx.x], flags_off, W, 2, me));
-  }
-}
-
-// Return address of every received row: its source rank's back buffer, at the source's
-// expert-major row.
-__global__ void ep_rowptr_kernel(const int32_t* __restrict__ seg_offsets,
-                                 const int32_t* __restrict__ recv_base,
-                                 const int32_t* __restrict__ src_off,
-                                 const uint64_t* __restrict__ peers, size_t back_off, int W,
-                                 int El, int64_t row_bytes, uint64_t* __restrict__ row_ptr) {
-  const int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int32_t R = seg_offsets[El];
-  if (r >= R) return;
-  int lo = 0, hi = El - 1;
-  while (lo < hi) {   // largest le with seg_offsets[le] <= r
-    const int mid = (lo + hi + 1) >> 1;
-    if (seg_offsets[mid] <= r) lo = mid; else hi = mid - 1;
-  }
-  const int le = lo;
-  int s = 0;
-  for (int q = 1; q < W; ++q)
-    if (recv_base[le * W + q] <= r) s = q;
-  const int64_t src_row = src_off[s * El + le] + (r - recv_base[le * W + s]);
-  row_ptr[r] = peers[s] + back_off + static_cast<uint64_t>(src_row * row_bytes);
-}
-
-// Dispatch: one warp per expert-major row of this rank, 16-byte stores into the owner's recv
-// buffer; the last block to finish publishes phase B on every peer.
-__global__ void __launch_bounds__(256)
-    ep_dispatch_kernel(const uint4* __restrict__ x, int64_t N, int k, int64_t vpr,
-                       const int64_t* __restrict__ ids, const int32_t* __restrict__ row_entry,
-                       const int32_t* __restrict__ expert_offsets,
-                       const int32_t* __restrict__ dst_base, int El,
-                       const uint64_t* __restrict__ peers, size_t recv_off,
-                       const uint64_t* __restrict__ flag_b, int W, int me, uint64_t epoch,
-                       unsigned int* __restrict__ done) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  // Rows are destination-major; start at the next rank's block so that, at any moment, the
-  // ranks write to different peers instead of all to the same one.
-  const int64_t shift = N > 0 ? expert_offsets[((me + 1) % W) * El] : 0;
-  for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; i < N;
-       i += warps) {
-    const int64_t q = (i + shift) % N;
-    const int32_t f = row_entry[q];
-    const int64_t e = ids[f];
-    const int64_t t = f / k;
-    const int d = static_cast<int>(e / El);
-    const int64_t dst_row = dst_base[e] + (q - expert_offsets[e]);
-    uint4* dst = reinterpret_cast<uint4*>(peers[d] + recv_off) + dst_row * vpr;
-    const uint4* src = x + t * vpr;
-    for (int64_t v = lane; v < vpr; v += 32 * 4) {
-      uint4 buf[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        if (v + 32 * u < vpr) buf[u] = src[v + 32 * u];
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        if (v + 32 * u < vpr) dst[v + 32 * u] = buf[u];
-    }
-  }
-  __threadfence_system();
   __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned int prev = atomicAdd(done, 1u);
-    if (prev == gridDim.x - 1) {
-      *done = 0u;
-      __threadfence_system();
-      for (int d = 0; d < W; ++d)
-        store_release_sys(reinterpret_cast<uint64_t*>(flag_b[d]), epoch);
+  // 5. where my rows of expert e start in its owner's receive layout
+  const int32_t mine = i < E ? C[me * E + i] : 0;
+  const int32_t my_ex = block_excl_scan(mine, E, tmp, nullptr);
+  if (i < E) tmp[i] = my_ex;
+  __syncthreads();
+  if (i < E) {
+    const int d = i / El;
+    const int jd = (d - me + W) % W;
+    int32_t base = my_ex - tmp[d * El];
+    for (int j = 0; j < jd; ++j) base += R[d * W + (d - j + W) % W];
+    dst_base[i] = base;
+  }
+  __syncthreads();
+  // 6. return address of each segment's first row: its source's back buffer, at the source's
+  //    expert-major row of its first row for my expert le
+  for (int s = 0; s < W; ++s) {
+    const int32_t c = i < E ? C[s * E + i] : 0;
+    const int32_t ex_s = block_excl_scan(c, E, tmp, nullptr);
+    if (i < E && i / El == me) {
+      const int j = (me - s + W) % W;
+      seg_base[j * El + (i - me * El)] =
+          peers[s] + back_off + static_cast<uint64_t>(ex_s) * static_cast<uint64_t>(row_bytes);
     }
   }
+  // 7. where this rank announces C (outputs landed) on each peer. The dispatch's chunk counter
+  //    starts at zero, and so do the next step's arrival counters (the other parity: every row
+  //    of the previous step was consumed by this rank's previous gate_up, and no peer adds to
+  //    the next step's before it has seen this rank's next A flag).
+  if (i == 0) *claim = 0u;
+  if (i < E) next_arrive[i] = 0u;
+  __threadfence_system();
+  if (i < W) flag_c[i] = reinterpret_cast<uint64_t>(flag_addr(peers[i], flags_off, W, 1, me));
 }
 
 __global__ void ep_wait_kernel(const uint64_t* __restrict__ peers, int me, size_t flags_off,
@@ -291,7 +244,9 @@ extern "C" {
 __attribute__((visibility("default"))) size_t prism_moe_ep_landing_bytes(
     int32_t ep_size, int64_t max_tokens, int32_t top_k, int64_t hidden, int32_t num_experts,
     int dtype) {
-  if (ep_size < 1 || max_tokens < 1 || top_k < 1 || hidden < 1 || num_experts < 1) return 0;
+  if (ep_size < 1 || ep_size > kMaxRanks || max_tokens < 1 || top_k < 1 || hidden < 1 ||
+      num_experts < 1 || num_experts > kMaxExperts)
+    return 0;
   return landing_layout(ep_size, max_tokens, top_k, hidden, num_experts,
                         dtype == PRISM_MOE_BF16 ? 2 : 4)
       .total;
@@ -302,7 +257,7 @@ __attribute__((visibility("default"))) int prism_moe_ep_alloc_landing(size_t byt
   PRISM_CHECK_ARG(bytes > 0 && ptr && ipc_handle, "ep_alloc_landing: bad arguments");
   void* p = nullptr;
   PRISM_CUDA(cudaMalloc(&p, bytes));
-  cudaError_t e = cudaMemset(p, 0, 4096 + 256);   // flags start at epoch 0
+  cudaError_t e = cudaMemset(p, 0, kHeaderBytes);   // flags at epoch 0, counters at 0
   if (e == cudaSuccess) {
     cudaIpcMemHandle_t h;
     e = cudaIpcGetMemHandle(&h, p);
@@ -402,47 +357,55 @@ __attribute__((visibility("default"))) int prism_moe_ep_forward(
   int r = build_plan(ids, T, k, E, 1, nullptr, nullptr, nullptr, counts, offsets, entry_row,
                      row_entry, ws + L.plan, L.plan_bytes, st);
   if (r) return r;
-  record_stage(2, st);   // exchange: counts all-gather, dispatch, wait for every source
+  record_stage(2, st);   // counts all-gather and the step's tables
   int32_t* seg_offsets = reinterpret_cast<int32_t*>(ws + L.seg_offsets);
+  int32_t* seg_expert = reinterpret_cast<int32_t*>(ws + L.seg_expert);
+  uint64_t* seg_base = reinterpret_cast<uint64_t*>(ws + L.seg_base);
   int32_t* dst_base = reinterpret_cast<int32_t*>(ws + L.dst_base);
-  int32_t* recv_base = reinterpret_cast<int32_t*>(ws + L.recv_base);
-  int32_t* src_off = reinterpret_cast<int32_t*>(ws + L.src_off);
-  uint64_t* flag_b = reinterpret_cast<uint64_t*>(ws + L.flag_b);
   uint64_t* flag_c = reinterpret_cast<uint64_t*>(ws + L.flag_c);
   unsigned int* done = reinterpret_cast<unsigned int*>(ws + L.done);
-  uint64_t* row_ptr = reinterpret_cast<uint64_t*>(ws + L.row_ptr);
-  const size_t counts_off = LL.counts;
   const size_t recv_off = LL.recv + static_cast<size_t>(par) * LL.rcap * hidden * es;
   const size_t back_off = LL.back + static_cast<size_t>(par) * LL.bcap * hidden * es;
-
-  ep_counts_kernel<<<1, 1024, 0, st>>>(counts, peer_landing, LL.flags, counts_off, W, me, E,
-                                       epoch, seg_offsets, dst_base, recv_base, src_off, flag_b,
-                                       flag_c, err);
-  PRISM_LAUNCH_CHECK("ep_counts_kernel launch");
-  ep_rowptr_kernel<<<static_cast<unsigned>(ceil_div(LL.rcap, 256)), 256, 0, st>>>(
-      seg_offsets, recv_base, src_off, peer_landing, back_off, W, El, hidden * es, row_ptr);
-  PRISM_LAUNCH_CHECK("ep_rowptr_kernel launch");
-  const unsigned dgrid = static_cast<unsigned>(std::max<int64_t>(
-      1, std::min<int64_t>(ceil_div(N, 8), static_cast<int64_t>(num_sms()) * 8)));
-  ep_dispatch_kernel<<<dgrid, 256, 0, st>>>(
-      static_cast<const uint4*>(x), N, k, hidden * es / 16, ids, row_entry, offsets, dst_base,
-      El, peer_landing, recv_off, flag_b, W, me, epoch, done);
-  PRISM_LAUNCH_CHECK("ep_dispatch_kernel launch");
-  ep_wait_kernel<<<1, 64, 0, st>>>(peer_landing, me, LL.flags, W, 1, epoch, err);
-  PRISM_LAUNCH_CHECK("ep_wait_kernel launch");
-  // expert GEMMs on the rows that landed here: gate_up locally, down with every row stored
-  // into its source rank's back buffer and completion signal C from the last CTA
   char* land = static_cast<char*>(my_landing);
+  const size_t arrive_off = LL.arrive + static_cast<size_t>(par) * E * sizeof(uint32_t);
+  uint32_t* next_arrive =
+      reinterpret_cast<uint32_t*>(land + LL.arrive + static_cast<size_t>(par ^ 1) * E * sizeof(uint32_t));
+
+  ep_counts_kernel<<<1, 1024, 0, st>>>(counts, peer_landing, LL.flags, LL.counts, back_off,
+                                       hidden * es, W, me, E, epoch, seg_offsets, seg_expert,
+                                       seg_base, dst_base, flag_c, next_arrive, done, err);
+  PRISM_LAUNCH_CHECK("ep_counts_kernel launch");
+  // One launch per GPU for the rest of the exchange and the experts: the gate_up GEMM's copy
+  // warps dispatch this rank's rows into the owners' receive buffers while its producer waits
+  // only for the sources whose rows the next tile reads; the down GEMM stores every output row
+  // into its source rank's back buffer and its last CTA signals C.
+  GemmDispatch disp{};
+  disp.x = x;
+  disp.vpr = hidden * es / 16;
+  disp.n_rows = N;
+  disp.k = k;
+  disp.ids = ids;
+  disp.row_entry = row_entry;
+  disp.expert_offsets = offsets;
+  disp.dst_base = dst_base;
+  disp.peers = peer_landing;
+  disp.recv_off = recv_off;
+  disp.arrive_off = arrive_off;
+  disp.my_arrive = reinterpret_cast<const uint32_t*>(land + arrive_off);
+  disp.claim = done;
+  disp.W = W;
+  disp.me = me;
+  disp.El = El;
   GemmOutput down{};
-  down.row_ptr = row_ptr;
+  down.seg_base = seg_base;
   down.signal_flags = reinterpret_cast<uint64_t* const*>(flag_c);
   down.num_signal = W;
   down.epoch = epoch;
   down.done_counter = done + 1;
-  r = expert_swiglu_bf16(land + recv_off, LL.rcap, hidden, inter, seg_offsets, nullptr, El, El,
-                         w_gate_up, w_down, nullptr, ws + L.h, err, st, &down);
+  r = expert_swiglu_bf16(land + recv_off, LL.rcap, hidden, inter, seg_offsets, seg_expert, E, El,
+                         w_gate_up, w_down, nullptr, ws + L.h, err, st, &down, &disp);
   if (r) return r;
-  ep_wait_kernel<<<1, 64, 0, st>>>(peer_landing, me, LL.flags, W, 2, epoch, err);
+  ep_wait_kernel<<<1, 64, 0, st>>>(peer_landing, me, LL.flags, W, 1, epoch, err);
   PRISM_LAUNCH_CHECK("ep_wait_kernel launch");
   r = combine(land + back_off, dtype, entry_row, w, T, k, hidden, out, st);
   record_stage(6, st);

@@ -40,7 +40,9 @@ namespace {
 
 constexpr int kBK = 64;   // 64 bf16 = 128 bytes = one swizzle row
 constexpr int kBN = 256;  // MMA N
-constexpr int kThreads = 192;
+constexpr int kThreads = 192;          // producer, MMA, 4 epilogue warps
+constexpr int kDispatchThreads = 320;  // + 4 copy warps when the EP dispatch runs in the launch
+constexpr uint64_t kPeerWaitNs = 10000000000ull;   // 10 s: peer ranks may start a step late
 constexpr uint32_t kTmemCols = 512;
 constexpr uint64_t kWaitNs = 2000000000ull;    // 2 s: far above any legitimate wait
 constexpr uint64_t kDrainNs = 100000000ull;    // 100 ms
@@ -85,15 +87,104 @@ __device__ __forceinline__ uint32_t swiglu_pair(uint32_t g0b, uint32_t g1b, uint
   return cvt_bf16x2(s0, s1);
 }
 
-template <int kMode, bool kPair>
-__global__ void __launch_bounds__(kThreads, 1)
+// Copy warp: ``n`` rows of expert ``e`` are written; publish them to the owner's arrival
+// counter of the receive segment they belong to.
+__device__ __forceinline__ void dispatch_flush(const GemmDispatch& D, int64_t e, unsigned int n,
+                                               int lane) {
+  __threadfence_system();
+  __syncwarp();
+  if (lane == 0) {
+    const int d = static_cast<int>(e / D.El);
+    const int j = (d - D.me + D.W) % D.W;
+    const int sg = j * D.El + static_cast<int>(e - static_cast<int64_t>(d) * D.El);
+    add_release_sys(reinterpret_cast<uint32_t*>(D.peers[d] + D.arrive_off) + sg, n);
+  }
+  __syncwarp();
+}
+
+// Copy warps of a dispatching gate_up launch: this rank's expert-major rows, own block first and
+// then the following ranks' blocks, in 16-row chunks that the copy warps claim from a shared
+// counter. Claiming (instead of a fixed chunk per CTA) lets the CTAs that are resident finish
+// every copy even when the GPU cannot hold the whole grid at once, so no peer waits on a CTA
+// that has not started. Lanes look up the chunk's 16 rows at once; rows then move two at a
+// time, 8 x 16 bytes per lane per row in flight.
+__device__ void dispatch_rows(const GemmDispatch& D, int lane) {
+  const int64_t N = D.n_rows;
+  if (N == 0) return;
+  constexpr int kChunkRows = 16;
+  constexpr int kVec = 8;   // 16-byte vectors per lane per row and pass
+  const int64_t shift = D.expert_offsets[D.me * D.El];
+  const int64_t nchunks = (N + kChunkRows - 1) / kChunkRows;
+  const int64_t vpr = D.vpr;
+  const uint4* x = static_cast<const uint4*>(D.x);
+  for (;;) {
+    unsigned int claimed = 0;
+    if (lane == 0) claimed = atomicAdd(D.claim, 1u);
+    const int64_t c = __shfl_sync(0xffffffffu, claimed, 0);
+    if (c >= nchunks) break;
+    const int64_t i0 = c * kChunkRows;
+    const int nr = static_cast<int>(N - i0 < kChunkRows ? N - i0 : kChunkRows);
+    // lane r < nr: row i0 + r -> source token, expert, and its address on the owner
+    int64_t my_e = -1, my_src = 0;
+    uint64_t my_dst = 0;
+    if (lane < nr) {
+      const int64_t q = (i0 + lane + shift) % N;
+      const int32_t f = D.row_entry[q];
+      my_e = D.ids[f];
+      my_src = f / D.k;
+      const int d = static_cast<int>(my_e / D.El);
+      const int64_t dst_row = D.dst_base[my_e] + (q - D.expert_offsets[my_e]);
+      my_dst = D.peers[d] + D.recv_off + static_cast<uint64_t>(dst_row * vpr * 16);
+    }
+    int64_t e_run = -1;
+    unsigned int n_run = 0;
+    for (int r = 0; r < nr; r += 2) {
+      const bool two = r + 1 < nr;
+      const int rb = two ? r + 1 : r;
+      const uint4* sa = x + __shfl_sync(0xffffffffu, my_src, r) * vpr;
+      const uint4* sb = x + __shfl_sync(0xffffffffu, my_src, rb) * vpr;
+      uint4* da = reinterpret_cast<uint4*>(__shfl_sync(0xffffffffu, my_dst, r));
+      uint4* db = reinterpret_cast<uint4*>(__shfl_sync(0xffffffffu, my_dst, rb));
+      for (int64_t v0 = 0; v0 < vpr; v0 += 32 * kVec) {
+        uint4 a[kVec], b[kVec];
+#pragma unroll
+        for (int u = 0; u < kVec; ++u) {
+          const int64_t v = v0 + lane + 32 * u;
+          if (v < vpr) a[u] = sa[v];
+          if (two && v < vpr) b[u] = sb[v];
+        }
+#pragma unroll
+        for (int u = 0; u < kVec; ++u) {
+          const int64_t v = v0 + lane + 32 * u;
+          if (v < vpr) da[v] = a[u];
+          if (two && v < vpr) db[v] = b[u];
+        }
+      }
+      // runs of one expert; a run's rows are all stored before its count is published
+      for (int t = r; t <= rb; ++t) {
+        const int64_t e = __shfl_sync(0xffffffffu, my_e, t);
+        if (e != e_run) {
+          if (n_run) dispatch_flush(D, e_run, n_run, lane);
+          e_run = e;
+          n_run = 0;
+        }
+        ++n_run;
+      }
+    }
+    if (n_run) dispatch_flush(D, e_run, n_run, lane);
+  }
+}
+
+template <int kMode, bool kPair, bool kDispatch>
+__global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
     grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
                               const __grid_constant__ CUtensorMap tmap_b,
                               const int32_t* __restrict__ seg_offsets,
                               const int32_t* __restrict__ seg_expert, int nseg, int num_kb,
                               int num_n_tiles, int64_t n_out, uint16_t* __restrict__ out,
                               int64_t out_ld, int32_t rows_cap, int* __restrict__ err,
-                              GemmOutput tgt) {
+                              GemmOutput tgt, GemmDispatch disp) {
+  static_assert(!kDispatch || (!kPair && kMode == kGateUp), "dispatch rides single gate_up");
   using C = Cfg<kPair>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -155,6 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0;
     uint32_t issued = 0;           // bit s: stage s has a load issued
     uint32_t issued_parity = 0;    // bit s: full-barrier parity of that load
+    int ready_seg = -1;            // dispatch: every row of this segment has landed
     bool ok = true;
     for (int64_t tile = unit; ok && tile < total_tiles; tile += num_units) {
       const int32_t mt = static_cast<int32_t>(tile / num_n_tiles);
@@ -162,6 +254,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int s = find_segment(prefix, nseg, mt);
       const int e = seg_expert ? seg_expert[s] : s;
       const int32_t row0 = seg_offsets[s] + (mt - prefix[s]) * C::kRows + 128 * rank;
+      if constexpr (kDispatch) {
+        // a CTA's tiles come in segment order: wait once per segment for all of its rows
+        if (s != ready_seg) {
+          const uint32_t need = static_cast<uint32_t>(seg_offsets[s + 1] - seg_offsets[s]);
+          const uint64_t t0 = global_timer_ns();
+          while (load_acquire_sys(disp.my_arrive + s) != need) {
+            if (*abort || global_timer_ns() - t0 > kPeerWaitNs) {
+              ok = false;
+              break;
+            }
+          }
+          if (!ok) break;
+          // rows written through the generic proxy (peer stores), read next by TMA
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          ready_seg = s;
+        }
+      }
       for (int kb = 0; kb < num_kb; ++kb) {
         if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort, kWaitNs)) {
           ok = false;
@@ -267,6 +376,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       volatile int never = 0;
       mbar_wait_bounded(drain, 0, &never, kDrainNs);
     }
+  } else if (kDispatch && warp >= 6) {
+    // ------------------------------------------------------------------ dispatch copy warps
+    dispatch_rows(disp, lane);
   } else if (warp >= 2) {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
@@ -294,9 +406,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // this lane's output row address (0 = no row): dense, or per-row (e.g. a peer GPU)
       uint64_t my_ptr = 0;
       if (row_in_tile < rows_valid)
-        my_ptr = tgt.row_ptr ? tgt.row_ptr[row0 + row_in_tile]
-                             : reinterpret_cast<uint64_t>(
-                                   out + static_cast<int64_t>(row0 + row_in_tile) * out_ld);
+        my_ptr = tgt.seg_base
+                     ? tgt.seg_base[s] + static_cast<uint64_t>(
+                                             (row0 + row_in_tile - seg_offsets[s]) * out_ld * 2)
+                     : reinterpret_cast<uint64_t>(
+                           out + static_cast<int64_t>(row0 + row_in_tile) * out_ld);
       // Each pass stages 32 rows x 64 columns in shared memory, then the warp writes 128-byte
       // row segments (8 lanes per row, 4 rows per instruction) — full NVLink / DRAM bursts
       // instead of 32 scattered 16-byte pieces.
@@ -422,12 +536,14 @@ int encode_bf16_map(CUtensorMap* map, const void* base, int rank, const uint64_t
   return PRISM_MOE_OK;
 }
 
-template <int kMode, bool kPair>
+template <int kMode, bool kPair, bool kDispatch = false>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const int32_t* seg_offsets,
                 const int32_t* seg_expert, int nseg, int64_t rows_cap, int64_t K, int64_t n_out,
-                uint16_t* out, int* err, const GemmOutput& tgt, cudaStream_t st) {
+                uint16_t* out, int* err, const GemmOutput& tgt, cudaStream_t st,
+                const GemmDispatch& disp = GemmDispatch{}) {
   using C = Cfg<kPair>;
-  auto kern = grouped_gemm_sm100_kernel<kMode, kPair>;
+  auto kern = grouped_gemm_sm100_kernel<kMode, kPair, kDispatch>;
+  constexpr int threads = kDispatch ? kDispatchThreads : kThreads;
   static std::once_flag once;
   static cudaError_t attr_status = cudaSuccess;
   static int max_units = 0;
@@ -444,7 +560,7 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const int32_t* seg
       attr[0].val.clusterDim.y = 1;
       attr[0].val.clusterDim.z = 1;
       cfg.gridDim = dim3(2 * (num_sms() / 2), 1, 1);
-      cfg.blockDim = dim3(kThreads, 1, 1);
+      cfg.blockDim = dim3(threads, 1, 1);
       cfg.dynamicSmemBytes = C::kSmemBytes;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
@@ -461,11 +577,15 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const int32_t* seg
   const int num_n_tiles = static_cast<int>(ceil_div(n_out, n_tile));
   const int num_kb = static_cast<int>(ceil_div(K, kBK));
   const int64_t max_tiles = (ceil_div(rows_cap, C::kRows) + nseg) * num_n_tiles;
-  const int units = static_cast<int>(std::min<int64_t>(max_units, std::max<int64_t>(max_tiles, 1)));
+  // a dispatching launch always spans every SM: its CTAs also carry the copy work, and one
+  // CTA per SM keeps them all resident together
+  const int units = kDispatch ? max_units
+                              : static_cast<int>(std::min<int64_t>(
+                                    max_units, std::max<int64_t>(max_tiles, 1)));
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   cfg.gridDim = dim3(static_cast<unsigned>(units * (kPair ? 2 : 1)), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = st;
   if (kPair) {
@@ -478,7 +598,7 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const int32_t* seg
   }
   PRISM_CUDA(cudaLaunchKernelEx(&cfg, kern, ma, mb, seg_offsets, seg_expert, nseg, num_kb,
                                 num_n_tiles, n_out, out, n_out, static_cast<int32_t>(rows_cap),
-                                err, tgt));
+                                err, tgt, disp));
   return PRISM_MOE_OK;
 }
 
@@ -496,7 +616,8 @@ bool use_pair(int64_t rows_cap, int nseg) {
 int expert_swiglu_bf16(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
                        const int32_t* seg_offsets, const int32_t* seg_expert, int nseg, int El,
                        const void* wgu, const void* wd, void* y, void* h, int* err,
-                       cudaStream_t st, const GemmOutput* down_out) {
+                       cudaStream_t st, const GemmOutput* down_out,
+                       const GemmDispatch* dispatch) {
   const GemmOutput dense{};
   const GemmOutput& down_tgt = down_out ? *down_out : dense;
   PRISM_CHECK_ARG(H % 8 == 0 && I % 8 == 0, "bf16 experts need hidden %% 8 == 0 and inter %% 8 == 0");
@@ -508,7 +629,8 @@ int expert_swiglu_bf16(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
                    reinterpret_cast<uintptr_t>(h)) % 16 == 0,
                   "bf16 expert operands must be 16-byte aligned");
   if (rows_cap == 0) return PRISM_MOE_OK;
-  const bool pair = use_pair(rows_cap, nseg);
+  // a dispatching step's capacity covers every source sending its maximum; it expects 1/W of it
+  const bool pair = use_pair(dispatch ? rows_cap / dispatch->W : rows_cap, nseg);
   CUtensorMap a1, b1, a2, b2;
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(H), static_cast<uint64_t>(rows_cap)};
@@ -542,10 +664,13 @@ int expert_swiglu_bf16(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
     if (r) return r;
   }
   record_stage(3, st);
-  int r = pair ? launch_gemm<kGateUp, true>(a1, b1, seg_offsets, seg_expert, nseg, rows_cap, H,
-                                            I, static_cast<uint16_t*>(h), err, dense, st)
-               : launch_gemm<kGateUp, false>(a1, b1, seg_offsets, seg_expert, nseg, rows_cap, H,
-                                             I, static_cast<uint16_t*>(h), err, dense, st);
+  int r = dispatch ? launch_gemm<kGateUp, false, true>(a1, b1, seg_offsets, seg_expert, nseg,
+                                                       rows_cap, H, I, static_cast<uint16_t*>(h),
+                                                       err, dense, st, *dispatch)
+          : pair   ? launch_gemm<kGateUp, true>(a1, b1, seg_offsets, seg_expert, nseg, rows_cap,
+                                                H, I, static_cast<uint16_t*>(h), err, dense, st)
+                   : launch_gemm<kGateUp, false>(a1, b1, seg_offsets, seg_expert, nseg, rows_cap,
+                                                 H, I, static_cast<uint16_t*>(h), err, dense, st);
   if (r) return r;
   record_stage(4, st);
   r = pair ? launch_gemm<kDown, true>(a2, b2, seg_offsets, seg_expert, nseg, rows_cap, I, H,

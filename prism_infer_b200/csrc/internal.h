@@ -9,15 +9,40 @@
 namespace prism {
 
 // Where a grouped GEMM writes its output rows and how it announces completion. Default: dense
-// rows ``out + r * ld``. With ``row_ptr``, row r goes to the address row_ptr[r] (any GPU's
-// memory reachable by peer access). With ``done_counter``, the last CTA to finish fences at
-// system scope and stores ``epoch`` to each of the ``num_signal`` flag addresses.
+// rows ``out + r * ld``. With ``seg_base``, row r of segment s goes to the address
+// seg_base[s] + (r - seg_offsets[s]) * ld * 2 (any GPU's memory reachable by peer access).
+// With ``done_counter``, the last CTA to finish fences at system scope and stores ``epoch`` to
+// each of the ``num_signal`` flag addresses.
 struct GemmOutput {
-  const uint64_t* row_ptr = nullptr;
+  const uint64_t* seg_base = nullptr;
   uint64_t* const* signal_flags = nullptr;
   int num_signal = 0;
   uint64_t epoch = 0;
   unsigned int* done_counter = nullptr;
+};
+
+// Expert-parallel dispatch carried out INSIDE the gate_up GEMM launch (ep.cu): extra copy warps
+// write this rank's expert-major rows into the owners' receive buffers, peers in rotated order
+// starting with this rank itself, and after each run of rows of one expert add the run's length
+// to that receive segment's arrival counter on the owner. The receive layout on rank d is
+// segment (j, le), index j * El + le = rows of local expert le from source (d - j) mod W. The
+// GEMM's producer waits (bounded) until the arrival counter of the segment a tile reads equals
+// the segment's row count.
+struct GemmDispatch {
+  const void* x = nullptr;              // [T, H] this rank's token rows
+  int64_t vpr = 0;                      // 16-byte vectors per row
+  int64_t n_rows = 0;                   // T * k routed rows
+  int k = 1;
+  const int64_t* ids = nullptr;         // [T*k] expert of each flat entry
+  const int32_t* row_entry = nullptr;   // [T*k] expert-major row -> flat entry
+  const int32_t* expert_offsets = nullptr;   // [E+1]
+  const int32_t* dst_base = nullptr;    // [E] first row of my expert-e rows in the owner's layout
+  const uint64_t* peers = nullptr;      // [W] landing-zone base addresses
+  size_t recv_off = 0;                  // byte offset of this step's receive buffer
+  size_t arrive_off = 0;                // byte offset of this step's [W*El] u32 arrival counters
+  const uint32_t* my_arrive = nullptr;  // the same counters in this rank's landing zone
+  unsigned int* claim = nullptr;        // next 16-row chunk to copy; zero at launch
+  int W = 1, me = 0, El = 1;
 };
 
 // route.cu
@@ -34,10 +59,12 @@ int permute_rows(const void* x, int64_t T, int64_t row_bytes, int k, const int32
 
 // expert_gemm_sm100.cu — records profiling stage slots 3, 4, 5. ``down_out`` (optional)
 // redirects the down GEMM's rows (y may then be NULL) and adds a completion signal.
+// ``dispatch`` (optional) runs the expert-parallel dispatch inside the gate_up launch.
 int expert_swiglu_bf16(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
                        const int32_t* seg_offsets, const int32_t* seg_expert, int nseg, int El,
                        const void* wgu, const void* wd, void* y, void* h, int* err,
-                       cudaStream_t st, const GemmOutput* down_out = nullptr);
+                       cudaStream_t st, const GemmOutput* down_out = nullptr,
+                       const GemmDispatch* dispatch = nullptr);
 
 // expert_gemm_simt.cu
 int expert_swiglu_f32(const float* x, int64_t rows_cap, int64_t H, int64_t I,
