@@ -62,8 +62,9 @@ def load_peaks():
     return FALLBACK_PEAKS, "fallback"
 
 
-def ncu_traffic():
-    """Per-launch DRAM bytes of the gate_up GEMM from the committed ncu summary, if any."""
+def ncu_traffic(kernel="gate_up"):
+    """Per-launch DRAM bytes of the dominant kernel (``gate_up`` or ``fused``) at config 2 from
+    the committed ncu summary, if it holds a figure for that kernel."""
     p = REPO / "profiles" / "ncu_traffic.txt"
     if not p.exists():
         return None
@@ -73,7 +74,7 @@ def ncu_traffic():
             k, v = line.split("=", 1)
             vals[k.strip()] = v.strip()
     try:
-        return float(vals["gate_up_cfg2_bytes_per_launch"])
+        return float(vals[f"{kernel}_cfg2_bytes_per_launch"])
     except (KeyError, ValueError):
         return None
 
@@ -125,6 +126,15 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
                 "samples": len(sm)}
+
+
+def launches_per_step(world, fused):
+    """This library's kernels per MoE.forward (the router GEMM is torch's): route, plan (chunk,
+    scan, scatter), then EP=1: permute, experts (2 launches, or 1 fused), combine; EP>1: counts
+    all-gather, the fused expert launch with the exchange inside, wait for returned rows,
+    combine."""
+    experts = 1 if fused else 2
+    return 1 + 3 + (1 + experts + 1 if world == 1 else 1 + experts + 1 + 1)
 
 
 def dist_setup(n):
@@ -291,8 +301,8 @@ def run_ours(args):
     moe.check_device_error(device) if world == 1 else None
 
     # per-stage averages (ms) — slots: route, plan, permute, gate_up, down, combine
-    # EP>1: "permute" is the exchange (counts all-gather, row dispatch over NVLink, wait for all
-    # sources) and "combine" includes waiting for the owners' down GEMMs to return every row
+    # EP>1: "exchange" is the counts all-gather; the row dispatch and return run inside the
+    # fused expert launch ("experts"), and "combine" includes waiting for every returned row
     names = ["route", "plan", "permute" if world == 1 else "exchange", "gate_up", "down",
              "combine"]
     stage_ms = {}
@@ -305,6 +315,10 @@ def run_ours(args):
                 pass
         stage_ms[name] = sum(vals) / len(vals) if vals else None
 
+    fused = stage_ms["down"] is not None and stage_ms["down"] < 5e-3
+    if fused:   # both expert GEMMs ran as one launch (slot 3 -> 4); slot 4 -> 5 is empty
+        stage_ms["experts"] = stage_ms.pop("gate_up")
+        stage_ms.pop("down")
     value = world * T * steps / (ms / 1e3)
 
     # ---- end to end through MoE.forward with host buffers ----
@@ -350,18 +364,27 @@ def run_ours(args):
     ms_e2e = time_device(e2e_step_timed, steps, max(2, warmup // 2), world)
     e2e_value = world * T * steps / (ms_e2e / 1e3)
 
-    # ---- roofline of the dominant kernel (gate_up grouped GEMM) ----
+    # ---- roofline of the dominant kernel ----
+    # fused engine (EP>1): both expert GEMMs in one launch, 6*H*I FLOP per routed row;
+    # otherwise the gate_up GEMM launch, 4*H*I FLOP per routed row
     rows = T * k                       # routed rows per rank (EP: received rows ~ T*k)
-    flops_gate_up = 2.0 * rows * H * (2 * I)
-    gu_ms = stage_ms["gate_up"]
-    achieved = flops_gate_up / (gu_ms / 1e3) / 1e12
+    if fused:
+        kflops = 2.0 * rows * H * (2 * I) + 2.0 * rows * I * H
+        kms = stage_ms["experts"]
+        kname = "fused_experts_kernel (gate_up + down, EP exchange inside)"
+        algo = f"2*{rows}*{H}*{2 * I} + 2*{rows}*{I}*{H} = {kflops:.4g} FLOP per launch"
+    else:
+        kflops = 2.0 * rows * H * (2 * I)
+        kms = stage_ms["gate_up"]
+        kname = "grouped_gemm_sm100_kernel<gate_up>"
+        algo = f"2*{rows}*{H}*{2 * I} = {kflops:.4g} FLOP per launch"
+    achieved = kflops / (kms / 1e3) / 1e12
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
-    traffic = ncu_traffic()
-    roofline = {"bound": "tensor", "kernel": "grouped_gemm_sm100_kernel<gate_up>",
+    traffic = ncu_traffic("fused" if fused else "gate_up")
+    roofline = {"bound": "tensor", "kernel": kname,
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "peak_source": f"{peak_kind} bf16_tflops (burst)",
-                "traffic": traffic,
-                "algorithmic": f"2*{rows}*{H}*{2 * I} = {flops_gate_up:.4g} FLOP per launch"}
+                "traffic": traffic, "algorithmic": algo}
     block_flops = T * world * (2 * H * E + k * 6 * H * I)
     extra = {
         "stages_ms": stage_ms,
@@ -425,7 +448,7 @@ def run_ours(args):
                 "d2h_bytes_per_step": T * H * 2,
                 "how": "MoE.forward; per step H2D of x from pinned host and D2H of the output, "
                        "on copy streams double-buffered against the forward"},
-        "gpu_launches": steps * 8,
+        "gpu_launches": steps * launches_per_step(world, fused),
         "clocks": clocks,
         **extra,
     }

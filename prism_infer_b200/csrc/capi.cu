@@ -79,7 +79,7 @@ BlockLayout block_layout(int64_t T, int64_t H, int64_t I, int E, int k, int dtyp
   L.offsets = take(sizeof(int32_t) * (E + 1));
   L.entry_row = take(sizeof(int32_t) * N);
   L.xs = take(es * N * H);
-  L.h = take(es * N * I);
+  L.h = take(expert_scratch_bytes(N, I, static_cast<int64_t>(es)));
   L.y = take(es * N * H);
   L.total = o;
   return L;
@@ -150,7 +150,7 @@ size_t prism_moe_expert_workspace_size(int64_t rows_capacity, int64_t hidden, in
                                        int dtype) {
   (void)hidden;
   if (rows_capacity < 0 || inter < 1 || !dtype_ok(dtype)) return 0;
-  return align_up(static_cast<size_t>(rows_capacity * inter * elem_size(dtype)), 256) + 256;
+  return expert_scratch_bytes(rows_capacity, inter, elem_size(dtype));
 }
 
 int prism_moe_expert_swiglu(const void* x_sorted, int dtype, int64_t rows_capacity,

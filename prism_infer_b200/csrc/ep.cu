@@ -18,11 +18,11 @@
 // peer's C flag of step i+1, which the peer raises only after its gate_up GEMM of step i+1 and
 // therefore after it finished reading step i's buffers.
 //
-// Step (prism_moe_ep_forward): route -> plan -> counts all-gather (A) and tables -> gate_up GEMM
-// whose copy warps dispatch the rows into the owners' recv buffers (B, one flag per source,
-// raised when that source's rows to this rank are all written) while its producer waits for
-// the B flag of the source each tile reads -> down GEMM whose epilogue stores every row into
-// its source rank's back buffer and signals C from its last CTA -> wait C -> local combine.
+// Step (prism_moe_ep_forward): route -> plan -> counts all-gather (A) and tables -> one fused
+// expert launch (expert_fused_sm100.cu) whose copy warps dispatch the rows into the owners'
+// recv buffers (per-segment arrival counters) while its producer waits only for the segment
+// each gate_up tile reads, and later forward the down GEMM's outputs into their source ranks'
+// back buffers; its last CTA signals C -> wait C -> local combine.
 // Every wait is bounded (kPeerWaitNs); a wait that runs out records PRISM_MOE_ERR_TIMEOUT.
 #include <algorithm>
 #include <cstring>
@@ -93,7 +93,7 @@ EpWs ep_ws_layout(int64_t max_tokens, int64_t H, int64_t I, int E, int k, int W,
   L.dst_base = take(sizeof(int32_t) * E);
   L.flag_c = take(sizeof(uint64_t) * W);
   L.done = take(sizeof(unsigned int) * 4);
-  L.h = take(static_cast<size_t>(es * rcap * I));
+  L.h = take(expert_scratch_bytes(rcap, I, es));
   L.total = o;
   return L;
 }
@@ -375,10 +375,10 @@ __attribute__((visibility("default"))) int prism_moe_ep_forward(
                                        hidden * es, W, me, E, epoch, seg_offsets, seg_expert,
                                        seg_base, dst_base, flag_c, next_arrive, done, err);
   PRISM_LAUNCH_CHECK("ep_counts_kernel launch");
-  // One launch per GPU for the rest of the exchange and the experts: the gate_up GEMM's copy
-  // warps dispatch this rank's rows into the owners' receive buffers while its producer waits
-  // only for the sources whose rows the next tile reads; the down GEMM stores every output row
-  // into its source rank's back buffer and its last CTA signals C.
+  // One launch per GPU for the rest of the exchange and the experts: its copy warps dispatch
+  // this rank's rows into the owners' receive buffers while its producer waits only for the
+  // segment the next gate_up tile reads, and forward every output row of another rank's
+  // segment into that rank's back buffer; its last CTA signals C.
   GemmDispatch disp{};
   disp.x = x;
   disp.vpr = hidden * es / 16;

@@ -1,0 +1,671 @@
+// Kernel 4b — both grouped SwiGLU expert GEMMs in ONE persistent launch (bf16, sm_100a).
+//
+// The gate_up and down GEMMs of expert_gemm_sm100.cu (same tiles: MMA M=128, N=256, K=16,
+// 4 stages of A 16 KB + B 32 KB, two 256-column fp32 accumulators in TMEM) run as one tile
+// stream that every CTA's producer claims from a global counter:
+//   gate_up tile (mt, nt): h[rows of m-tile mt, 128 columns nt] = silu(x Wg^T) * (x Wu^T)
+//   down tile    (mt, nt): y[rows of m-tile mt, 256 columns nt] = h Wd^T
+// The stream interleaves the two kinds: after the gate_up tiles of the first L m-tiles, each
+// step emits the gate_up tiles of m-tile r and the down tiles of m-tile r - L, so a down tile
+// is claimed L steps (several hundred tiles) after the gate_up tiles it reads. Each gate_up
+// epilogue warp publishes its stored h rows on a per-m-tile counter (release, GPU scope); the
+// producer of a down tile waits (bounded) for that counter before its TMA reads h. Tiles are
+// claimed in stream order by CTAs that are running and every dependency points to an earlier
+// claim, so the launch makes progress even when the GPU holds fewer CTAs than the grid.
+//
+// With expert parallelism (``GemmDispatch``) four more warps per CTA move the rows across
+// NVLink inside the same launch:
+//   dispatch  this rank's expert-major rows into the owners' receive buffers, 16-row chunks,
+//             peers in rotated order, each run of one expert's rows published on the owner's
+//             per-segment arrival counter (release, system scope); the producer of a gate_up
+//             tile waits for its segment's counter;
+//   return    the down GEMM's output rows of other ranks' segments, staged by the epilogue in
+//             place of the m-tile's (consumed) input rows, stored into the source rank's buffer
+//             32 rows at a time as soon as an m-tile's down tiles are done (items dealt
+//             round-robin to the copy warps, which interleave them with dispatch chunks).
+// The epilogue therefore only writes local memory, and both transfers overlap tensor-core work.
+//
+// Warp roles: warp 0 lane 0 claims tiles, publishes each to a shared-memory ring (8 entries,
+// full/empty mbarriers) and issues the TMA loads; warp 1 lane 0 issues the MMAs; warps 2..5
+// drain the accumulators; warps 6..9 (expert parallelism only) copy rows. Every wait is bounded.
+#include <algorithm>
+#include <cstdlib>
+#include <mutex>
+
+#include "gemm_sm100.cuh"
+
+namespace prism {
+namespace {
+
+struct FusedCfg {
+  static constexpr int kStages = 4;
+  static constexpr int kABytes = 128 * kBK * 2;
+  static constexpr int kBBytes = kBN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kTxBytes = kStageBytes;
+  static constexpr uint32_t kIdesc = idesc_bf16_f32(128, kBN);
+  static constexpr int kRing = 8;
+  static constexpr size_t kBarOffset = static_cast<size_t>(kStages) * kStageBytes;
+  static constexpr size_t kBarBytes = 512;
+  static constexpr size_t kPrefixOffset = kBarOffset + kBarBytes;
+  static constexpr size_t kStageOutOffset = kPrefixOffset + kPrefixBytes;
+  static constexpr size_t kSmemBytes = 1024 + kStageOutOffset + 4 * 32 * kStageRowBytes;
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+  // full, empty, acc_full, acc_empty, ring_full, ring_empty, drain + ring, tmem slot, abort
+  static_assert((2 * kStages + 4 + 2 * kRing + 1) * 8 + kRing * 4 + 8 <= kBarBytes,
+                "barrier area");
+};
+
+struct FusedParams {
+  const int32_t* seg_offsets = nullptr;
+  const int32_t* seg_expert = nullptr;
+  int nseg = 0;
+  int32_t rows_cap = 0;
+  int n_gu = 0;    // gate_up n-tiles: ceil(I / 128)
+  int n_dn = 0;    // down n-tiles: ceil(H / 256)
+  int kb_gu = 0;   // gate_up k-blocks: ceil(H / 64)
+  int kb_dn = 0;   // down k-blocks: ceil(I / 64)
+  int lag = 1;     // L, in m-tiles
+  int64_t H = 0, I = 0;
+  uint16_t* xs = nullptr;              // [rows_cap, H] gate_up input rows
+  uint16_t* h = nullptr;               // [rows_cap, I]
+  uint16_t* y = nullptr;               // [rows_cap, H] unless the output has seg_base
+  unsigned int* claim = nullptr;       // tile claim counter, zero at launch
+  unsigned int* h_ready = nullptr;     // per m-tile: gate_up epilogue warps done, zero at launch
+  unsigned int* y_ready = nullptr;     // per m-tile: down epilogue warps done, zero at launch
+  int* err = nullptr;
+};
+
+struct TileRef {
+  int kind;     // 0 gate_up, 1 down
+  int32_t mt;
+  int nt;
+};
+
+// Position c of the interleaved tile stream over M m-tiles.
+__device__ __forceinline__ TileRef tile_at(int32_t c, int32_t M, int nG, int nD, int L) {
+  const int32_t A = M < L ? M : L;
+  if (c < nG * A) return {0, c / nG, c % nG};
+  c -= nG * A;
+  const int per = nG + nD;
+  const int32_t mid = M > L ? M - L : 0;
+  if (c < per * mid) {
+    const int32_t r = L + c / per;
+    const int o = c % per;
+    return o < nG ? TileRef{0, r, o} : TileRef{1, r - L, o - nG};
+  }
+  c -= per * mid;
+  const int32_t first = M > L ? M - L : 0;
+  return {1, first + c / nD, c % nD};
+}
+
+__device__ __forceinline__ uint32_t load_acquire_gpu(const unsigned int* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void add_release_gpu(unsigned int* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// ---------------------------------------------------------------------------------------------
+// copy warps (expert parallelism)
+// ---------------------------------------------------------------------------------------------
+// Dispatch: ``n`` rows of expert ``e`` are written; publish them to the owner's arrival counter
+// of the receive segment they belong to.
+__device__ __forceinline__ void dispatch_flush(const GemmDispatch& D, int64_t e, unsigned int n,
+                                               int lane) {
+  __threadfence_system();
+  __syncwarp();
+  if (lane == 0) {
+    const int d = static_cast<int>(e / D.El);
+    const int j = (d - D.me + D.W) % D.W;
+    const int sg = j * D.El + static_cast<int>(e - static_cast<int64_t>(d) * D.El);
+    add_release_sys(reinterpret_cast<uint32_t*>(D.peers[d] + D.arrive_off) + sg, n);
+  }
+  __syncwarp();
+}
+
+// Copy one or two rows of ``vpr`` 16-byte vectors, 8 vectors per lane per row in flight.
+__device__ __forceinline__ void copy_row_pair(const uint4* sa, uint4* da, const uint4* sb,
+                                              uint4* db, bool two, int64_t vpr, int lane) {
+  constexpr int kVec = 8;
+  for (int64_t v0 = 0; v0 < vpr; v0 += 32 * kVec) {
+    uint4 a[kVec], b[kVec];
+#pragma unroll
+    for (int u = 0; u < kVec; ++u) {
+      const int64_t v = v0 + lane + 32 * u;
+      if (v < vpr) a[u] = sa[v];
+      if (two && v < vpr) b[u] = sb[v];
+    }
+#pragma unroll
+    for (int u = 0; u < kVec; ++u) {
+      const int64_t v = v0 + lane + 32 * u;
+      if (v < vpr) da[v] = a[u];
+      if (two && v < vpr) db[v] = b[u];
+    }
+  }
+}
+
+// One 16-row dispatch chunk of this rank's expert-major rows, own block first and then the
+// following ranks' blocks. Lanes look up the chunk's rows at once; rows then move in pairs.
+__device__ void dispatch_chunk(const GemmDispatch& D, int64_t c, int lane) {
+  constexpr int kChunkRows = 16;
+  const int64_t N = D.n_rows;
+  const int64_t shift = D.expert_offsets[D.me * D.El];
+  const int64_t i0 = c * kChunkRows;
+  const int nr = static_cast<int>(N - i0 < kChunkRows ? N - i0 : kChunkRows);
+  const uint4* x = static_cast<const uint4*>(D.x);
+  int64_t my_e = -1, my_src = 0;
+  uint64_t my_dst = 0;
+  if (lane < nr) {
+    const int64_t q = (i0 + lane + shift) % N;
+    const int32_t f = D.row_entry[q];
+    my_e = D.ids[f];
+    my_src = f / D.k;
+    const int d = static_cast<int>(my_e / D.El);
+    const int64_t dst_row = D.dst_base[my_e] + (q - D.expert_offsets[my_e]);
+    my_dst = D.peers[d] + D.recv_off + static_cast<uint64_t>(dst_row * D.vpr * 16);
+  }
+  int64_t e_run = -1;
+  unsigned int n_run = 0;
+  for (int r = 0; r < nr; r += 2) {
+    const bool two = r + 1 < nr;
+    const int rb = two ? r + 1 : r;
+    copy_row_pair(x + __shfl_sync(0xffffffffu, my_src, r) * D.vpr,
+                  reinterpret_cast<uint4*>(__shfl_sync(0xffffffffu, my_dst, r)),
+                  x + __shfl_sync(0xffffffffu, my_src, rb) * D.vpr,
+                  reinterpret_cast<uint4*>(__shfl_sync(0xffffffffu, my_dst, rb)), two, D.vpr,
+                  lane);
+    // runs of one expert; a run's rows are all stored before its count is published
+    for (int t = r; t <= rb; ++t) {
+      const int64_t e = __shfl_sync(0xffffffffu, my_e, t);
+      if (e != e_run) {
+        if (n_run) dispatch_flush(D, e_run, n_run, lane);
+        e_run = e;
+        n_run = 0;
+      }
+      ++n_run;
+    }
+  }
+  if (n_run) dispatch_flush(D, e_run, n_run, lane);
+}
+
+// Return: rows [32 q, 32 q + 32) of m-tile mt (a segment of another rank) of down-GEMM output,
+// staged in place of the m-tile's input rows, stored into the source rank's buffer.
+__device__ void return_quarter(const FusedParams& P, const GemmOutput& tgt,
+                               const int32_t* prefix, int32_t mt, int q, int lane) {
+  const int s = find_segment(prefix, P.nseg, mt);
+  const int32_t row0 = P.seg_offsets[s] + (mt - prefix[s]) * 128 + 32 * q;
+  const int32_t end = P.seg_offsets[s + 1] < P.rows_cap ? P.seg_offsets[s + 1] : P.rows_cap;
+  const int nr = end - row0 < 32 ? end - row0 : 32;
+  const int64_t vpr = P.H / 8;
+  const uint64_t base = tgt.seg_base[s];
+  for (int r = 0; r < nr; r += 2) {
+    const bool two = r + 1 < nr;
+    const int64_t ra = row0 + r, rb = row0 + (two ? r + 1 : r);
+    copy_row_pair(reinterpret_cast<const uint4*>(P.xs + ra * P.H),
+                  reinterpret_cast<uint4*>(
+                      base + static_cast<uint64_t>((ra - P.seg_offsets[s]) * P.H * 2)),
+                  reinterpret_cast<const uint4*>(P.xs + rb * P.H),
+                  reinterpret_cast<uint4*>(
+                      base + static_cast<uint64_t>((rb - P.seg_offsets[s]) * P.H * 2)),
+                  two, vpr, lane);
+  }
+}
+
+// Copy-warp loop. Return items (32 rows each, in m-tile order) are dealt round-robin to the
+// grid's copy warps; a warp forwards its next item as soon as that m-tile's down tiles are
+// stored, and otherwise takes the next dispatch chunk from the shared counter. Each warp polls
+// only its own item's counter (with backoff), so no single address is hammered by every warp.
+__device__ void copy_warp_loop(const GemmDispatch& D, const FusedParams& P,
+                               const GemmOutput& tgt, const int32_t* prefix, int32_t M,
+                               volatile int* abort, int cw, int n_cw, int lane) {
+  constexpr int kChunkRows = 16;
+  const int64_t nchunks = (D.n_rows + kChunkRows - 1) / kChunkRows;
+  const int32_t m0 = prefix[D.El];   // m-tiles from here on hold rows of other ranks
+  const int64_t n_ret = static_cast<int64_t>(M - m0) * 4;
+  const uint32_t y_target = 4u * static_cast<uint32_t>(P.n_dn);
+  bool dispatch_left = nchunks > 0;
+  int64_t item = cw;
+  uint64_t idle_since = 0;
+  uint32_t backoff = 64;
+  for (;;) {
+    if (item < n_ret) {
+      int ready = 0;
+      if (lane == 0)
+        ready = load_acquire_gpu(P.y_ready + m0 + static_cast<int32_t>(item / 4)) == y_target;
+      if (__shfl_sync(0xffffffffu, ready, 0)) {
+        return_quarter(P, tgt, prefix, m0 + static_cast<int32_t>(item / 4),
+                       static_cast<int>(item & 3), lane);
+        item += n_cw;
+        idle_since = 0;
+        backoff = 64;
+        continue;
+      }
+    }
+    if (dispatch_left) {
+      unsigned int claimed = 0;
+      if (lane == 0) claimed = atomicAdd(D.claim, 1u);
+      const int64_t c = __shfl_sync(0xffffffffu, claimed, 0);
+      if (c < nchunks) {
+        dispatch_chunk(D, c, lane);
+        idle_since = 0;
+        continue;
+      }
+      dispatch_left = false;
+    }
+    if (item >= n_ret) break;
+    // this warp's next return item is not stored yet: wait (bounded)
+    if (idle_since == 0) idle_since = global_timer_ns();
+    if (*abort || global_timer_ns() - idle_since > kPeerWaitNs) {
+      *abort = 1;
+      record_device_error(P.err, PRISM_MOE_ERR_TIMEOUT);
+      break;
+    }
+    __nanosleep(backoff);
+    if (backoff < 2048) backoff <<= 1;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------------------------
+template <bool kDispatch>
+__global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
+    fused_experts_kernel(const __grid_constant__ CUtensorMap map_x,
+                         const __grid_constant__ CUtensorMap map_wgu,
+                         const __grid_constant__ CUtensorMap map_h,
+                         const __grid_constant__ CUtensorMap map_wd, FusedParams P,
+                         GemmOutput tgt, GemmDispatch disp) {
+  using F = FusedCfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* stages = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + F::kBarOffset);
+  uint64_t* empty = full + F::kStages;
+  uint64_t* acc_full = empty + F::kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* ring_full = acc_empty + 2;
+  uint64_t* ring_empty = ring_full + F::kRing;
+  uint64_t* drain = ring_empty + F::kRing;
+  int32_t* ring_tile = reinterpret_cast<int32_t*>(drain + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring_tile + F::kRing);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int32_t* prefix = reinterpret_cast<int32_t*>(smem + F::kPrefixOffset);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < F::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    for (int i = 0; i < F::kRing; ++i) {
+      mbar_init(&ring_full[i], 1);
+      mbar_init(&ring_empty[i], 5);   // the MMA thread and the 4 epilogue warps
+    }
+    mbar_init(drain, 1);
+    *abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&map_x);
+    tma_prefetch_desc(&map_wgu);
+    tma_prefetch_desc(&map_h);
+    tma_prefetch_desc(&map_wd);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 2) build_tile_prefix(P.seg_offsets, P.nseg, 128, prefix);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int32_t M = prefix[P.nseg];
+  const int32_t total = M * (P.n_gu + P.n_dn);
+  const uint32_t h_target = 4u * static_cast<uint32_t>(P.n_gu);
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------------ scheduler + TMA
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued = 0, issued_parity = 0;
+    int rslot = 0;
+    uint32_t rphase = 0;
+    int ready_seg = -1;      // dispatch: every row of this segment has landed
+    int32_t ready_mt = -1;   // every h row of this m-tile is stored
+    bool ok = true;
+    for (;;) {
+      int32_t t = -1;
+      {
+        const unsigned int c = atomicAdd(P.claim, 1u);
+        if (c < static_cast<unsigned int>(total)) t = static_cast<int32_t>(c);
+      }
+      if (!mbar_wait_bounded(&ring_empty[rslot], rphase ^ 1, abort, kWaitNs)) {
+        ok = false;
+        break;
+      }
+      ring_tile[rslot] = t;
+      mbar_arrive(&ring_full[rslot]);
+      if (++rslot == F::kRing) {
+        rslot = 0;
+        rphase ^= 1;
+      }
+      if (t < 0) break;
+      const TileRef tr = tile_at(t, M, P.n_gu, P.n_dn, P.lag);
+      const int s = find_segment(prefix, P.nseg, tr.mt);
+      const int e = P.seg_expert ? P.seg_expert[s] : s;
+      const int32_t row0 = P.seg_offsets[s] + (tr.mt - prefix[s]) * 128;
+      const uint64_t t0 = global_timer_ns();
+      if (tr.kind == 0) {
+        if (kDispatch && s != ready_seg) {
+          const uint32_t need = static_cast<uint32_t>(P.seg_offsets[s + 1] - P.seg_offsets[s]);
+          while (load_acquire_sys(disp.my_arrive + s) != need) {
+            if (*abort || global_timer_ns() - t0 > kPeerWaitNs) {
+              ok = false;
+              break;
+            }
+          }
+          // rows written through the generic proxy (peer stores), read next by TMA
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          ready_seg = s;
+        }
+      } else if (tr.mt != ready_mt) {
+        while (load_acquire_gpu(P.h_ready + tr.mt) != h_target) {
+          if (*abort || global_timer_ns() - t0 > kWaitNs) {
+            ok = false;
+            break;
+          }
+        }
+        asm volatile("fence.proxy.async.global;" ::: "memory");   // h: generic stores -> TMA
+        ready_mt = tr.mt;
+      }
+      if (!ok) break;
+      const int nkb = tr.kind == 0 ? P.kb_gu : P.kb_dn;
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort, kWaitNs)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sa = stages + stage * F::kStageBytes;
+        uint8_t* sb = sa + F::kABytes;
+        mbar_arrive_expect_tx(&full[stage], F::kTxBytes);
+        if (tr.kind == 0) {
+          tma_load_2d(sa, &map_x, &full[stage], kb * kBK, row0);
+          // gate rows then up rows of n-tile nt in one copy (box spans both halves)
+          tma_load_4d(sb, &map_wgu, &full[stage], kb * kBK, tr.nt * 128, 0, e);
+        } else {
+          tma_load_2d(sa, &map_h, &full[stage], kb * kBK, row0);
+          tma_load_3d(sb, &map_wd, &full[stage], kb * kBK, tr.nt * kBN, e);
+        }
+        issued |= 1u << stage;
+        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == F::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+    }
+    if (!ok) {
+      *abort = 1;
+      record_device_error(P.err, PRISM_MOE_ERR_TIMEOUT);
+      for (int s = 0; s < F::kStages; ++s)   // every issued copy lands before the CTA exits
+        if ((issued >> s) & 1u) {
+          volatile int never = 0;
+          mbar_wait_bounded(&full[s], (issued_parity >> s) & 1u, &never, kDrainNs);
+        }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------------ MMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    int rslot = 0;
+    uint32_t rphase = 0;
+    bool ok = true;
+    for (int it = 0;; ++it) {
+      if (!mbar_wait_bounded(&ring_full[rslot], rphase, abort, kWaitNs)) {
+        ok = false;
+        break;
+      }
+      const int32_t t = ring_tile[rslot];
+      mbar_arrive(&ring_empty[rslot]);
+      if (++rslot == F::kRing) {
+        rslot = 0;
+        rphase ^= 1;
+      }
+      if (t < 0) break;
+      const int nkb = tile_at(t, M, P.n_gu, P.n_dn, P.lag).kind == 0 ? P.kb_gu : P.kb_dn;
+      const int buf = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait_bounded(&acc_empty[buf], acc_phase ^ 1, abort, kWaitNs)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + buf * kBN;
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!mbar_wait_bounded(&full[stage], phase, abort, kWaitNs)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(stages + stage * F::kStageBytes);
+        const uint32_t b0 = a0 + F::kABytes;
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)
+          tc_mma_bf16(d_tmem, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32),
+                      F::kIdesc, (kb | kk) != 0 ? 1u : 0u);
+        tc_commit(&empty[stage]);
+        if (++stage == F::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      tc_commit(&acc_full[buf]);
+    }
+    if (!ok) {
+      *abort = 1;
+      record_device_error(P.err, PRISM_MOE_ERR_TIMEOUT);
+    }
+    if (*abort) {
+      tc_commit(drain);   // completes once every MMA issued above has finished
+      volatile int never = 0;
+      mbar_wait_bounded(drain, 0, &never, kDrainNs);
+    }
+  } else if (kDispatch && warp >= 6) {
+    // ------------------------------------------------------------------ copy warps
+    copy_warp_loop(disp, P, tgt, prefix, M, abort, static_cast<int>(blockIdx.x) * 4 + (warp - 6),
+                   static_cast<int>(gridDim.x) * 4, lane);
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp & 3;                 // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;  // row within the tile
+    uint8_t* stage_out = smem + F::kStageOutOffset + (warp - 2) * 32 * kStageRowBytes;
+    int rslot = 0;
+    uint32_t rphase = 0;
+    for (int it = 0;; ++it) {
+      if (!mbar_wait_bounded(&ring_full[rslot], rphase, abort, kWaitNs)) {
+        *abort = 1;
+        record_device_error(P.err, PRISM_MOE_ERR_TIMEOUT);
+        break;
+      }
+      const int32_t t = ring_tile[rslot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ring_empty[rslot]);
+      if (++rslot == F::kRing) {
+        rslot = 0;
+        rphase ^= 1;
+      }
+      if (t < 0) break;
+      const TileRef tr = tile_at(t, M, P.n_gu, P.n_dn, P.lag);
+      const int buf = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      const int s = find_segment(prefix, P.nseg, tr.mt);
+      const int32_t row0 = P.seg_offsets[s] + (tr.mt - prefix[s]) * 128;
+      const int32_t seg_end = P.seg_offsets[s + 1];
+      const int32_t rows_valid = (seg_end < P.rows_cap ? seg_end : P.rows_cap) - row0;
+      if (!mbar_wait_bounded(&acc_full[buf], acc_phase, abort, kWaitNs)) {
+        *abort = 1;
+        record_device_error(P.err, PRISM_MOE_ERR_TIMEOUT);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * kBN;
+      const bool has_row = row_in_tile < rows_valid;
+      const int64_t row = row0 + row_in_tile;
+      if (tr.kind == 0) {
+        const uint64_t my_ptr = has_row ? reinterpret_cast<uint64_t>(P.h + row * P.I) : 0;
+        drain_tile<true>(taddr, my_ptr, stage_out, lane, static_cast<int64_t>(tr.nt) * 128,
+                         P.I);
+        // publish this warp's 32 h rows to the producers of the m-tile's down tiles
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) add_release_gpu(P.h_ready + tr.mt, 1u);
+      } else {
+        // rows of another rank's segment are staged in place of the m-tile's input rows (all
+        // of its gate_up tiles are done) and forwarded by the copy warps
+        const bool staged = kDispatch && s >= disp.El;
+        uint64_t my_ptr = 0;
+        if (has_row)
+          my_ptr = staged ? reinterpret_cast<uint64_t>(P.xs + row * P.H)
+                   : tgt.seg_base
+                       ? tgt.seg_base[s] +
+                             static_cast<uint64_t>((row - P.seg_offsets[s]) * P.H * 2)
+                       : reinterpret_cast<uint64_t>(P.y + row * P.H);
+        drain_tile<false>(taddr, my_ptr, stage_out, lane, static_cast<int64_t>(tr.nt) * kBN,
+                          P.H);
+        if (staged) {
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) add_release_gpu(P.y_ready + tr.mt, 1u);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  if (tgt.done_counter != nullptr && warp >= 2) __threadfence_system();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+  // completion signal: the last CTA to get here publishes `epoch` to every flag
+  if (tgt.done_counter != nullptr && threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned int prev = atomicAdd(tgt.done_counter, 1u);
+    if (prev == gridDim.x - 1) {
+      *tgt.done_counter = 0u;  // ready for the next launch (stream-ordered)
+      __threadfence_system();
+      for (int i = 0; i < tgt.num_signal; ++i) store_release_sys(tgt.signal_flags[i], tgt.epoch);
+    }
+  }
+}
+
+template <bool kDispatch>
+int launch_fused(const CUtensorMap (&maps)[4], const FusedParams& P, const GemmOutput& tgt,
+                 const GemmDispatch& disp, int grid, cudaStream_t st) {
+  auto kern = fused_experts_kernel<kDispatch>;
+  static std::once_flag once;
+  static cudaError_t attr_status = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_status = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(FusedCfg::kSmemBytes));
+  });
+  PRISM_CUDA(attr_status);
+  kern<<<grid, kDispatch ? kDispatchThreads : kThreads, FusedCfg::kSmemBytes, st>>>(
+      maps[0], maps[1], maps[2], maps[3], P, tgt, disp);
+  PRISM_LAUNCH_CHECK("fused_experts_kernel launch");
+  return PRISM_MOE_OK;
+}
+
+int64_t max_mtiles(int64_t rows_cap) { return ceil_div(rows_cap, 128) + kMaxSegments; }
+
+}  // namespace
+
+// [0] tile claim, [1] unused, h_ready[max m-tiles], y_ready[max m-tiles]
+size_t fused_sync_bytes(int64_t rows_cap) {
+  return sizeof(unsigned int) * static_cast<size_t>(2 + 2 * max_mtiles(rows_cap));
+}
+
+int expert_swiglu_fused(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
+                        const int32_t* seg_offsets, const int32_t* seg_expert, int nseg, int El,
+                        const void* wgu, const void* wd, void* y, void* h, unsigned int* sync,
+                        int* err, cudaStream_t st, const GemmOutput* down_out,
+                        const GemmDispatch* dispatch) {
+  PRISM_CHECK_ARG(!dispatch || (down_out && down_out->seg_base),
+                  "fused experts: a dispatching step needs per-segment return addresses");
+  CUtensorMap maps[4];
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(H), static_cast<uint64_t>(rows_cap)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(H) * 2};
+    const uint32_t box[2] = {kBK, 128};
+    int r = encode_bf16_map(&maps[0], xs, 2, dims, strides, box);
+    if (r) return r;
+  }
+  {
+    const uint64_t dims[4] = {static_cast<uint64_t>(H), static_cast<uint64_t>(I), 2,
+                              static_cast<uint64_t>(El)};
+    const uint64_t strides[3] = {static_cast<uint64_t>(H) * 2, static_cast<uint64_t>(I * H) * 2,
+                                 static_cast<uint64_t>(2 * I * H) * 2};
+    const uint32_t box[4] = {kBK, 128, 2, 1};   // gate and up halves of an n-tile
+    int r = encode_bf16_map(&maps[1], wgu, 4, dims, strides, box);
+    if (r) return r;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(I), static_cast<uint64_t>(rows_cap)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(I) * 2};
+    const uint32_t box[2] = {kBK, 128};
+    int r = encode_bf16_map(&maps[2], h, 2, dims, strides, box);
+    if (r) return r;
+  }
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(I), static_cast<uint64_t>(H),
+                              static_cast<uint64_t>(El)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(I) * 2, static_cast<uint64_t>(H * I) * 2};
+    const uint32_t box[3] = {kBK, kBN, 1};
+    int r = encode_bf16_map(&maps[3], wd, 3, dims, strides, box);
+    if (r) return r;
+  }
+  const int grid = num_sms();
+  FusedParams P;
+  P.seg_offsets = seg_offsets;
+  P.seg_expert = seg_expert;
+  P.nseg = nseg;
+  P.rows_cap = static_cast<int32_t>(rows_cap);
+  P.n_gu = static_cast<int>(ceil_div(I, 128));
+  P.n_dn = static_cast<int>(ceil_div(H, kBN));
+  P.kb_gu = static_cast<int>(ceil_div(H, kBK));
+  P.kb_dn = static_cast<int>(ceil_div(I, kBK));
+  // A CTA holds up to about three tiles between claiming one and storing its output; a lag of
+  // twice that keeps down tiles from waiting for h even when epilogues run slow.
+  P.lag = static_cast<int>(std::max<int64_t>(1, ceil_div(6 * grid, P.n_gu + P.n_dn)));
+  if (const char* lg = std::getenv("PRISM_MOE_FUSED_LAG")) P.lag = std::max(1, std::atoi(lg));
+  P.H = H;
+  P.I = I;
+  P.xs = static_cast<uint16_t*>(const_cast<void*>(xs));
+  P.h = static_cast<uint16_t*>(h);
+  P.y = static_cast<uint16_t*>(y);
+  P.claim = sync;
+  P.h_ready = sync + 2;
+  P.y_ready = sync + 2 + max_mtiles(rows_cap);
+  P.err = err;
+  PRISM_CUDA(cudaMemsetAsync(sync, 0, fused_sync_bytes(rows_cap), st));
+  const GemmOutput dense{};
+  const GemmOutput& tgt = down_out ? *down_out : dense;
+  return dispatch ? launch_fused<true>(maps, P, tgt, *dispatch, grid, st)
+                  : launch_fused<false>(maps, P, tgt, GemmDispatch{}, grid, st);
+}
+
+}  // namespace prism

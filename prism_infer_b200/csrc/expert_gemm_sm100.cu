@@ -32,159 +32,20 @@
 #include <cstdlib>
 #include <mutex>
 
-#include "internal.h"
-#include "segments.cuh"
+#include "gemm_sm100.cuh"
 
 namespace prism {
 namespace {
 
-constexpr int kBK = 64;   // 64 bf16 = 128 bytes = one swizzle row
-constexpr int kBN = 256;  // MMA N
-constexpr int kThreads = 192;          // producer, MMA, 4 epilogue warps
-constexpr int kDispatchThreads = 320;  // + 4 copy warps when the EP dispatch runs in the launch
-constexpr uint64_t kPeerWaitNs = 10000000000ull;   // 10 s: peer ranks may start a step late
-constexpr uint32_t kTmemCols = 512;
-constexpr uint64_t kWaitNs = 2000000000ull;    // 2 s: far above any legitimate wait
-constexpr uint64_t kDrainNs = 100000000ull;    // 100 ms
-constexpr int kStageRowBytes = 64 * 2 + 16;   // epilogue staging: 64 bf16 + 16 B pad per row
-constexpr size_t kPrefixBytes = ((kMaxSegments + 1) * 4 + 15) / 16 * 16;
-
-template <bool kPair>
-struct Cfg {
-  static constexpr int kRows = kPair ? 256 : 128;           // rows per tile
-  static constexpr int kABytes = 128 * kBK * 2;              // this CTA's A rows
-  static constexpr int kBBytes = (kPair ? 128 : 256) * kBK * 2;   // this CTA's B rows
-  static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = kPair ? 6 : 4;
-  static constexpr uint32_t kTxBytes = (kPair ? 2 : 1) * kStageBytes;   // per full barrier
-  static constexpr uint32_t kIdesc = idesc_bf16_f32(kRows, kBN);
-  static constexpr size_t kStageOutOffset =
-      static_cast<size_t>(kStages) * kStageBytes + 256 + kPrefixBytes;
-  static constexpr size_t kSmemBytes = 1024 + kStageOutOffset + 4 * 32 * kStageRowBytes;
-  static_assert(kSmemBytes <= 232448, "shared memory budget");
-};
-
-enum : int { kGateUp = 0, kDown = 1 };
-
-// Two fp32 values -> packed bf16x2 (round to nearest even) in one instruction; lo in bits 0-15.
-__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
-  uint32_t r;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  return r;
-}
-
-// SwiGLU of one (gate, up) pair of fp32 accumulators: both rounded to bf16 first (the reference
-// materialises gate_up in bf16), then silu(g) * u = g*u / (1 + e^-g) in fp32 with the fast
-// exponential and reciprocal — the result is rounded to bf16, far coarser than their error.
-__device__ __forceinline__ uint32_t swiglu_pair(uint32_t g0b, uint32_t g1b, uint32_t u0b,
-                                                uint32_t u1b) {
-  const uint32_t gp = cvt_bf16x2(__uint_as_float(g0b), __uint_as_float(g1b));
-  const uint32_t up = cvt_bf16x2(__uint_as_float(u0b), __uint_as_float(u1b));
-  const float g0 = __uint_as_float(gp << 16), g1 = __uint_as_float(gp & 0xffff0000u);
-  const float u0 = __uint_as_float(up << 16), u1 = __uint_as_float(up & 0xffff0000u);
-  const float s0 = __fdividef(g0 * u0, 1.0f + __expf(-g0));
-  const float s1 = __fdividef(g1 * u1, 1.0f + __expf(-g1));
-  return cvt_bf16x2(s0, s1);
-}
-
-// Copy warp: ``n`` rows of expert ``e`` are written; publish them to the owner's arrival
-// counter of the receive segment they belong to.
-__device__ __forceinline__ void dispatch_flush(const GemmDispatch& D, int64_t e, unsigned int n,
-                                               int lane) {
-  __threadfence_system();
-  __syncwarp();
-  if (lane == 0) {
-    const int d = static_cast<int>(e / D.El);
-    const int j = (d - D.me + D.W) % D.W;
-    const int sg = j * D.El + static_cast<int>(e - static_cast<int64_t>(d) * D.El);
-    add_release_sys(reinterpret_cast<uint32_t*>(D.peers[d] + D.arrive_off) + sg, n);
-  }
-  __syncwarp();
-}
-
-// Copy warps of a dispatching gate_up launch: this rank's expert-major rows, own block first and
-// then the following ranks' blocks, in 16-row chunks that the copy warps claim from a shared
-// counter. Claiming (instead of a fixed chunk per CTA) lets the CTAs that are resident finish
-// every copy even when the GPU cannot hold the whole grid at once, so no peer waits on a CTA
-// that has not started. Lanes look up the chunk's 16 rows at once; rows then move two at a
-// time, 8 x 16 bytes per lane per row in flight.
-__device__ void dispatch_rows(const GemmDispatch& D, int lane) {
-  const int64_t N = D.n_rows;
-  if (N == 0) return;
-  constexpr int kChunkRows = 16;
-  constexpr int kVec = 8;   // 16-byte vectors per lane per row and pass
-  const int64_t shift = D.expert_offsets[D.me * D.El];
-  const int64_t nchunks = (N + kChunkRows - 1) / kChunkRows;
-  const int64_t vpr = D.vpr;
-  const uint4* x = static_cast<const uint4*>(D.x);
-  for (;;) {
-    unsigned int claimed = 0;
-    if (lane == 0) claimed = atomicAdd(D.claim, 1u);
-    const int64_t c = __shfl_sync(0xffffffffu, claimed, 0);
-    if (c >= nchunks) break;
-    const int64_t i0 = c * kChunkRows;
-    const int nr = static_cast<int>(N - i0 < kChunkRows ? N - i0 : kChunkRows);
-    // lane r < nr: row i0 + r -> source token, expert, and its address on the owner
-    int64_t my_e = -1, my_src = 0;
-    uint64_t my_dst = 0;
-    if (lane < nr) {
-      const int64_t q = (i0 + lane + shift) % N;
-      const int32_t f = D.row_entry[q];
-      my_e = D.ids[f];
-      my_src = f / D.k;
-      const int d = static_cast<int>(my_e / D.El);
-      const int64_t dst_row = D.dst_base[my_e] + (q - D.expert_offsets[my_e]);
-      my_dst = D.peers[d] + D.recv_off + static_cast<uint64_t>(dst_row * vpr * 16);
-    }
-    int64_t e_run = -1;
-    unsigned int n_run = 0;
-    for (int r = 0; r < nr; r += 2) {
-      const bool two = r + 1 < nr;
-      const int rb = two ? r + 1 : r;
-      const uint4* sa = x + __shfl_sync(0xffffffffu, my_src, r) * vpr;
-      const uint4* sb = x + __shfl_sync(0xffffffffu, my_src, rb) * vpr;
-      uint4* da = reinterpret_cast<uint4*>(__shfl_sync(0xffffffffu, my_dst, r));
-      uint4* db = reinterpret_cast<uint4*>(__shfl_sync(0xffffffffu, my_dst, rb));
-      for (int64_t v0 = 0; v0 < vpr; v0 += 32 * kVec) {
-        uint4 a[kVec], b[kVec];
-#pragma unroll
-        for (int u = 0; u < kVec; ++u) {
-          const int64_t v = v0 + lane + 32 * u;
-          if (v < vpr) a[u] = sa[v];
-          if (two && v < vpr) b[u] = sb[v];
-        }
-#pragma unroll
-        for (int u = 0; u < kVec; ++u) {
-          const int64_t v = v0 + lane + 32 * u;
-          if (v < vpr) da[v] = a[u];
-          if (two && v < vpr) db[v] = b[u];
-        }
-      }
-      // runs of one expert; a run's rows are all stored before its count is published
-      for (int t = r; t <= rb; ++t) {
-        const int64_t e = __shfl_sync(0xffffffffu, my_e, t);
-        if (e != e_run) {
-          if (n_run) dispatch_flush(D, e_run, n_run, lane);
-          e_run = e;
-          n_run = 0;
-        }
-        ++n_run;
-      }
-    }
-    if (n_run) dispatch_flush(D, e_run, n_run, lane);
-  }
-}
-
-template <int kMode, bool kPair, bool kDispatch>
-__global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
+template <int kMode, bool kPair>
+__global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
                               const __grid_constant__ CUtensorMap tmap_b,
                               const int32_t* __restrict__ seg_offsets,
                               const int32_t* __restrict__ seg_expert, int nseg, int num_kb,
                               int num_n_tiles, int64_t n_out, uint16_t* __restrict__ out,
                               int64_t out_ld, int32_t rows_cap, int* __restrict__ err,
-                              GemmOutput tgt, GemmDispatch disp) {
-  static_assert(!kDispatch || (!kPair && kMode == kGateUp), "dispatch rides single gate_up");
+                              GemmOutput tgt) {
   using C = Cfg<kPair>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -246,7 +107,6 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
     uint32_t phase = 0;
     uint32_t issued = 0;           // bit s: stage s has a load issued
     uint32_t issued_parity = 0;    // bit s: full-barrier parity of that load
-    int ready_seg = -1;            // dispatch: every row of this segment has landed
     bool ok = true;
     for (int64_t tile = unit; ok && tile < total_tiles; tile += num_units) {
       const int32_t mt = static_cast<int32_t>(tile / num_n_tiles);
@@ -254,23 +114,6 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
       const int s = find_segment(prefix, nseg, mt);
       const int e = seg_expert ? seg_expert[s] : s;
       const int32_t row0 = seg_offsets[s] + (mt - prefix[s]) * C::kRows + 128 * rank;
-      if constexpr (kDispatch) {
-        // a CTA's tiles come in segment order: wait once per segment for all of its rows
-        if (s != ready_seg) {
-          const uint32_t need = static_cast<uint32_t>(seg_offsets[s + 1] - seg_offsets[s]);
-          const uint64_t t0 = global_timer_ns();
-          while (load_acquire_sys(disp.my_arrive + s) != need) {
-            if (*abort || global_timer_ns() - t0 > kPeerWaitNs) {
-              ok = false;
-              break;
-            }
-          }
-          if (!ok) break;
-          // rows written through the generic proxy (peer stores), read next by TMA
-          asm volatile("fence.proxy.async.global;" ::: "memory");
-          ready_seg = s;
-        }
-      }
       for (int kb = 0; kb < num_kb; ++kb) {
         if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort, kWaitNs)) {
           ok = false;
@@ -290,8 +133,8 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
         } else {
           tma_load_2d(sa, &tmap_a, &full[stage], kb * kBK, row0);
           if constexpr (kMode == kGateUp) {
+            // gate rows then up rows of n-tile nt in one copy (box spans both halves)
             tma_load_4d(sb, &tmap_b, &full[stage], kb * kBK, nt * 128, 0, e);
-            tma_load_4d(sb + C::kBBytes / 2, &tmap_b, &full[stage], kb * kBK, nt * 128, 1, e);
           } else {
             tma_load_3d(sb, &tmap_b, &full[stage], kb * kBK, nt * kBN, e);
           }
@@ -376,9 +219,6 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
       volatile int never = 0;
       mbar_wait_bounded(drain, 0, &never, kDrainNs);
     }
-  } else if (kDispatch && warp >= 6) {
-    // ------------------------------------------------------------------ dispatch copy warps
-    dispatch_rows(disp, lane);
   } else if (warp >= 2) {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
@@ -411,55 +251,9 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
                                              (row0 + row_in_tile - seg_offsets[s]) * out_ld * 2)
                      : reinterpret_cast<uint64_t>(
                            out + static_cast<int64_t>(row0 + row_in_tile) * out_ld);
-      // Each pass stages 32 rows x 64 columns in shared memory, then the warp writes 128-byte
-      // row segments (8 lanes per row, 4 rows per instruction) — full NVLink / DRAM bursts
-      // instead of 32 scattered 16-byte pieces.
-      constexpr int kPassCols = 64;
-      constexpr int kOutCols = kMode == kGateUp ? 128 : kBN;
-#pragma unroll 1
-      for (int cc = 0; cc < kOutCols; cc += kPassCols) {
-#pragma unroll 1
-        for (int c = 0; c < kPassCols; c += 32) {   // 32 columns per tcgen05.wait::ld
-          __syncwarp();
-          uint32_t packed[16];
-          if constexpr (kMode == kGateUp) {
-            uint32_t g[32], u[32];
-            tmem_ld16(taddr + cc + c, *reinterpret_cast<uint32_t(*)[16]>(&g[0]));
-            tmem_ld16(taddr + cc + c + 16, *reinterpret_cast<uint32_t(*)[16]>(&g[16]));
-            tmem_ld16(taddr + 128 + cc + c, *reinterpret_cast<uint32_t(*)[16]>(&u[0]));
-            tmem_ld16(taddr + 128 + cc + c + 16, *reinterpret_cast<uint32_t(*)[16]>(&u[16]));
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              packed[i] = swiglu_pair(g[2 * i], g[2 * i + 1], u[2 * i], u[2 * i + 1]);
-          } else {
-            uint32_t v[32];
-            tmem_ld16(taddr + cc + c, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
-            tmem_ld16(taddr + cc + c + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              packed[i] = cvt_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
-          }
-          uint4* srow = reinterpret_cast<uint4*>(stage_out + lane * kStageRowBytes + c * 2);
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4)
-            srow[q4] = make_uint4(packed[4 * q4], packed[4 * q4 + 1], packed[4 * q4 + 2],
-                                  packed[4 * q4 + 3]);
-        }
-        __syncwarp();
-        const int64_t col_base = static_cast<int64_t>(nt) * kOutCols + cc;
-        const int seg = lane & 7;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int r = (lane >> 3) + 4 * j;
-          const uint64_t p = __shfl_sync(0xffffffffu, my_ptr, r);
-          const int64_t col = col_base + seg * 8;
-          if (p != 0 && col + 8 <= n_out)
-            *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p) + col) =
-                *reinterpret_cast<const uint4*>(stage_out + r * kStageRowBytes + seg * 16);
-        }
-      }
+      drain_tile<kMode == kGateUp>(taddr, my_ptr, stage_out, lane,
+                                   static_cast<int64_t>(nt) * (kMode == kGateUp ? 128 : kBN),
+                                   n_out);
       tc_fence_before();
       if constexpr (kPair)
         mbar_arrive_cluster(acc_empty_leader + buf * 8);
@@ -511,6 +305,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
+}  // namespace
+
 int encode_bf16_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                     const uint64_t* stride_bytes, const uint32_t* box) {
   auto enc = tensor_map_encoder();
@@ -536,14 +332,15 @@ int encode_bf16_map(CUtensorMap* map, const void* base, int rank, const uint64_t
   return PRISM_MOE_OK;
 }
 
-template <int kMode, bool kPair, bool kDispatch = false>
+namespace {
+
+template <int kMode, bool kPair>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const int32_t* seg_offsets,
                 const int32_t* seg_expert, int nseg, int64_t rows_cap, int64_t K, int64_t n_out,
-                uint16_t* out, int* err, const GemmOutput& tgt, cudaStream_t st,
-                const GemmDispatch& disp = GemmDispatch{}) {
+                uint16_t* out, int* err, const GemmOutput& tgt, cudaStream_t st) {
   using C = Cfg<kPair>;
-  auto kern = grouped_gemm_sm100_kernel<kMode, kPair, kDispatch>;
-  constexpr int threads = kDispatch ? kDispatchThreads : kThreads;
+  auto kern = grouped_gemm_sm100_kernel<kMode, kPair>;
+  constexpr int threads = kThreads;
   static std::once_flag once;
   static cudaError_t attr_status = cudaSuccess;
   static int max_units = 0;
@@ -577,11 +374,8 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const int32_t* seg
   const int num_n_tiles = static_cast<int>(ceil_div(n_out, n_tile));
   const int num_kb = static_cast<int>(ceil_div(K, kBK));
   const int64_t max_tiles = (ceil_div(rows_cap, C::kRows) + nseg) * num_n_tiles;
-  // a dispatching launch always spans every SM: its CTAs also carry the copy work, and one
-  // CTA per SM keeps them all resident together
-  const int units = kDispatch ? max_units
-                              : static_cast<int>(std::min<int64_t>(
-                                    max_units, std::max<int64_t>(max_tiles, 1)));
+  const int units =
+      static_cast<int>(std::min<int64_t>(max_units, std::max<int64_t>(max_tiles, 1)));
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   cfg.gridDim = dim3(static_cast<unsigned>(units * (kPair ? 2 : 1)), 1, 1);
@@ -598,17 +392,23 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const int32_t* seg
   }
   PRISM_CUDA(cudaLaunchKernelEx(&cfg, kern, ma, mb, seg_offsets, seg_expert, nseg, num_kb,
                                 num_n_tiles, n_out, out, n_out, static_cast<int32_t>(rows_cap),
-                                err, tgt, disp));
+                                err, tgt));
   return PRISM_MOE_OK;
 }
 
+enum class Engine { kFused, kSingle, kPair };
+
 // Pair tiles (256 rows) pay off once segments are long: tail tiles waste up to 255 rows per
-// segment, single tiles up to 127. PRISM_MOE_GEMM_ENGINE=single|pair overrides the choice.
-bool use_pair(int64_t rows_cap, int nseg) {
+// segment, single tiles up to 127. A dispatching step runs both GEMMs as one fused launch
+// (expert_fused_sm100.cu), so that the dispatch and the down GEMM's stores into peers overlap
+// tensor-core work. PRISM_MOE_GEMM_ENGINE=fused|single|pair overrides the choice for steps
+// without a dispatch (single = two launches with 128-row tiles).
+Engine pick_engine(int64_t rows_cap, int nseg, bool dispatch) {
   const char* force = std::getenv("PRISM_MOE_GEMM_ENGINE");
-  if (force && force[0] == 's') return false;
-  if (force && force[0] == 'p') return true;
-  return rows_cap / std::max(nseg, 1) >= 2048;
+  if (dispatch || (force && force[0] == 'f')) return Engine::kFused;
+  if (force && force[0] == 's') return Engine::kSingle;
+  if (force && force[0] == 'p') return Engine::kPair;
+  return rows_cap / std::max(nseg, 1) >= 2048 ? Engine::kPair : Engine::kSingle;
 }
 
 }  // namespace
@@ -629,8 +429,16 @@ int expert_swiglu_bf16(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
                    reinterpret_cast<uintptr_t>(h)) % 16 == 0,
                   "bf16 expert operands must be 16-byte aligned");
   if (rows_cap == 0) return PRISM_MOE_OK;
-  // a dispatching step's capacity covers every source sending its maximum; it expects 1/W of it
-  const bool pair = use_pair(dispatch ? rows_cap / dispatch->W : rows_cap, nseg);
+  const Engine engine = pick_engine(rows_cap, nseg, dispatch != nullptr);
+  if (engine == Engine::kFused) {
+    record_stage(3, st);
+    int r = expert_swiglu_fused(xs, rows_cap, H, I, seg_offsets, seg_expert, nseg, El, wgu, wd,
+                                y, h, fused_sync(h, rows_cap, I), err, st, down_out, dispatch);
+    record_stage(4, st);   // one launch: slot 3 -> 4 covers both GEMMs, 4 -> 5 is empty
+    record_stage(5, st);
+    return r;
+  }
+  const bool pair = engine == Engine::kPair;
   CUtensorMap a1, b1, a2, b2;
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(H), static_cast<uint64_t>(rows_cap)};
@@ -644,7 +452,8 @@ int expert_swiglu_bf16(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
                               static_cast<uint64_t>(El)};
     const uint64_t strides[3] = {static_cast<uint64_t>(H) * 2, static_cast<uint64_t>(I * H) * 2,
                                  static_cast<uint64_t>(2 * I * H) * 2};
-    const uint32_t box[4] = {kBK, 128, 1, 1};
+    // single tiles take both halves (gate, up) of an n-tile per copy; a pair CTA one half
+    const uint32_t box[4] = {kBK, 128, pair ? 1u : 2u, 1};
     int r = encode_bf16_map(&b1, wgu, 4, dims, strides, box);
     if (r) return r;
   }
@@ -664,10 +473,7 @@ int expert_swiglu_bf16(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
     if (r) return r;
   }
   record_stage(3, st);
-  int r = dispatch ? launch_gemm<kGateUp, false, true>(a1, b1, seg_offsets, seg_expert, nseg,
-                                                       rows_cap, H, I, static_cast<uint16_t*>(h),
-                                                       err, dense, st, *dispatch)
-          : pair   ? launch_gemm<kGateUp, true>(a1, b1, seg_offsets, seg_expert, nseg, rows_cap,
+  int r = pair ? launch_gemm<kGateUp, true>(a1, b1, seg_offsets, seg_expert, nseg, rows_cap,
                                                 H, I, static_cast<uint16_t*>(h), err, dense, st)
                    : launch_gemm<kGateUp, false>(a1, b1, seg_offsets, seg_expert, nseg, rows_cap,
                                                  H, I, static_cast<uint16_t*>(h), err, dense, st);

@@ -21,13 +21,14 @@ struct GemmOutput {
   unsigned int* done_counter = nullptr;
 };
 
-// Expert-parallel dispatch carried out INSIDE the gate_up GEMM launch (ep.cu): extra copy warps
+// Expert-parallel exchange carried out INSIDE the fused expert launch (ep.cu): extra copy warps
 // write this rank's expert-major rows into the owners' receive buffers, peers in rotated order
 // starting with this rank itself, and after each run of rows of one expert add the run's length
 // to that receive segment's arrival counter on the owner. The receive layout on rank d is
 // segment (j, le), index j * El + le = rows of local expert le from source (d - j) mod W. The
 // GEMM's producer waits (bounded) until the arrival counter of the segment a tile reads equals
-// the segment's row count.
+// the segment's row count. The same copy warps later forward the down GEMM's output rows of
+// other ranks' segments to their sources (GemmOutput::seg_base).
 struct GemmDispatch {
   const void* x = nullptr;              // [T, H] this rank's token rows
   int64_t vpr = 0;                      // 16-byte vectors per row
@@ -57,14 +58,34 @@ int build_plan(const int64_t* ids, int64_t T, int k, int E, int W, int64_t* perm
 int permute_rows(const void* x, int64_t T, int64_t row_bytes, int k, const int32_t* entry_row,
                  void* xs, cudaStream_t st);
 
-// expert_gemm_sm100.cu — records profiling stage slots 3, 4, 5. ``down_out`` (optional)
-// redirects the down GEMM's rows (y may then be NULL) and adds a completion signal.
-// ``dispatch`` (optional) runs the expert-parallel dispatch inside the gate_up launch.
+// Scratch of the expert GEMMs: h [rows_cap, I] (element size es), then (bf16) the fused
+// launch's counters, which it zeroes itself before every launch.
+size_t fused_sync_bytes(int64_t rows_cap);
+inline size_t expert_scratch_bytes(int64_t rows_cap, int64_t I, int64_t es) {
+  const size_t hb = (static_cast<size_t>(es * rows_cap * I) + 255) / 256 * 256;
+  return hb + (fused_sync_bytes(rows_cap) + 255) / 256 * 256;
+}
+inline unsigned int* fused_sync(void* scratch, int64_t rows_cap, int64_t I) {
+  return reinterpret_cast<unsigned int*>(static_cast<char*>(scratch) +
+                                         (static_cast<size_t>(2 * rows_cap * I) + 255) / 256 * 256);
+}
+
+// expert_gemm_sm100.cu — records profiling stage slots 3, 4 (two-launch engines only), 5.
+// ``h`` is the scratch above. ``down_out`` (optional) redirects the down GEMM's rows (y may
+// then be NULL) and adds a completion signal. ``dispatch`` (optional) runs the expert-parallel
+// dispatch and return copies inside the fused launch.
 int expert_swiglu_bf16(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
                        const int32_t* seg_offsets, const int32_t* seg_expert, int nseg, int El,
                        const void* wgu, const void* wd, void* y, void* h, int* err,
                        cudaStream_t st, const GemmOutput* down_out = nullptr,
                        const GemmDispatch* dispatch = nullptr);
+
+// expert_fused_sm100.cu — both GEMMs in one persistent launch (single 128-row tiles).
+int expert_swiglu_fused(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
+                        const int32_t* seg_offsets, const int32_t* seg_expert, int nseg, int El,
+                        const void* wgu, const void* wd, void* y, void* h, unsigned int* sync,
+                        int* err, cudaStream_t st, const GemmOutput* down_out,
+                        const GemmDispatch* dispatch);
 
 // expert_gemm_simt.cu
 int expert_swiglu_f32(const float* x, int64_t rows_cap, int64_t H, int64_t I,

@@ -168,14 +168,18 @@ def _segments(counts, device=DEV):
     (64, 32, [5, 9, 1]),                           # K and N smaller than one tile
     (320, 200, [129, 64]),                         # K, N not multiples of the tile
     (4096, 1536, [300]),                           # Qwen3-235B-A22B expert shape
+    (1024, 512, [2000, 1500, 0, 2100, 1999, 2001, 1]),   # more m-tiles than the fused lag
 ])
-@pytest.mark.parametrize("dtype,engine", [(torch.bfloat16, "single"), (torch.bfloat16, "pair"),
-                                          (torch.float32, "simt")])
+@pytest.mark.parametrize("dtype,engine", [(torch.bfloat16, "fused"), (torch.bfloat16, "single"),
+                                          (torch.bfloat16, "pair"), (torch.float32, "simt")])
 def test_expert_swiglu_matches_oracle(H, I, counts, dtype, engine, monkeypatch):
-    """``engine``: bf16 tcgen05 single-CTA tiles (128 rows) or CTA-pair tiles (256 rows,
+    """``engine``: bf16 tcgen05 with both GEMMs in one persistent launch (128-row tiles), two
+    launches of single-CTA tiles (128 rows), or two launches of CTA-pair tiles (256 rows,
     cta_group::2); fp32 runs on CUDA cores."""
     if dtype == torch.float32 and H * I > 2048 * 768:
         pytest.skip("fp32 CUDA-core path is exercised at the smaller shapes")
+    if dtype == torch.float32 and sum(counts) > 5000:
+        pytest.skip("fp32 CUDA-core path is exercised at the smaller row counts")
     if dtype == torch.bfloat16:
         monkeypatch.setenv("PRISM_MOE_GEMM_ENGINE", engine)
     gen = torch.Generator(device=DEV).manual_seed(H + I + len(counts))
@@ -207,7 +211,7 @@ def test_expert_swiglu_matches_oracle(H, I, counts, dtype, engine, monkeypatch):
             np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-5)
 
 
-@pytest.mark.parametrize("engine", ["single", "pair"])
+@pytest.mark.parametrize("engine", ["fused", "single", "pair"])
 def test_expert_swiglu_segment_expert_map(engine, monkeypatch):
     """Segments may name any local expert (EP receiver layout: (source rank, local expert))."""
     monkeypatch.setenv("PRISM_MOE_GEMM_ENGINE", engine)
