@@ -21,8 +21,8 @@
 // Step (prism_moe_ep_forward): route -> plan -> counts all-gather (A) and tables -> one fused
 // expert launch (expert_fused_sm100.cu) whose copy warps dispatch the rows into the owners'
 // recv buffers (per-segment arrival counters) while its producer waits only for the segment
-// each gate_up tile reads, and later forward the down GEMM's outputs into their source ranks'
-// back buffers; its last CTA signals C -> wait C -> local combine.
+// each gate_up tile reads, and whose down epilogue stores every output row into its source
+// rank's back buffer; its last CTA signals C -> wait C -> local combine.
 // Every wait is bounded (kPeerWaitNs); a wait that runs out records PRISM_MOE_ERR_TIMEOUT.
 #include <algorithm>
 #include <cstring>
@@ -377,8 +377,8 @@ __attribute__((visibility("default"))) int prism_moe_ep_forward(
   PRISM_LAUNCH_CHECK("ep_counts_kernel launch");
   // One launch per GPU for the rest of the exchange and the experts: its copy warps dispatch
   // this rank's rows into the owners' receive buffers while its producer waits only for the
-  // segment the next gate_up tile reads, and forward every output row of another rank's
-  // segment into that rank's back buffer; its last CTA signals C.
+  // segment the next gate_up tile reads; the down epilogue stores every output row into its
+  // source rank's back buffer, and the last CTA signals C.
   GemmDispatch disp{};
   disp.x = x;
   disp.vpr = hidden * es / 16;

@@ -13,21 +13,21 @@
 // claimed in stream order by CTAs that are running and every dependency points to an earlier
 // claim, so the launch makes progress even when the GPU holds fewer CTAs than the grid.
 //
-// With expert parallelism (``GemmDispatch``) four more warps per CTA move the rows across
-// NVLink inside the same launch:
-//   dispatch  this rank's expert-major rows into the owners' receive buffers, 16-row chunks,
-//             peers in rotated order, each run of one expert's rows published on the owner's
-//             per-segment arrival counter (release, system scope); the producer of a gate_up
-//             tile waits for its segment's counter;
-//   return    the down GEMM's output rows of other ranks' segments, staged by the epilogue in
-//             place of the m-tile's (consumed) input rows, stored into the source rank's buffer
-//             32 rows at a time as soon as an m-tile's down tiles are done (items dealt
-//             round-robin to the copy warps, which interleave them with dispatch chunks).
-// The epilogue therefore only writes local memory, and both transfers overlap tensor-core work.
+// With expert parallelism (``GemmDispatch``) four more warps per CTA dispatch this rank's
+// expert-major rows into the owners' receive buffers inside the same launch: 16-row chunks
+// claimed from a shared counter, peers in rotated order, each run of one expert's rows
+// published on the owner's per-segment arrival counter (release, system scope); the producer
+// of a gate_up tile waits for its segment's counter. The down epilogue stores every output row
+// straight into its source rank's buffer (GemmOutput::seg_base, 128-byte segments over NVLink),
+// so both transfers overlap tensor-core work. (Forwarding the outputs through the copy warps
+// instead, staged in local memory, measured slower at 2 and 4 GPUs.)
 //
 // Warp roles: warp 0 lane 0 claims tiles, publishes each to a shared-memory ring (8 entries,
 // full/empty mbarriers) and issues the TMA loads; warp 1 lane 0 issues the MMAs; warps 2..5
 // drain the accumulators; warps 6..9 (expert parallelism only) copy rows. Every wait is bounded.
+// The measured comparison with two launches (expert_gemm_sm100.cu): on one GPU the two
+// launches are faster (every CTA works on one weight stream at a time), with an exchange the
+// fused launch is.
 #include <algorithm>
 #include <cstdlib>
 #include <mutex>
@@ -67,12 +67,10 @@ struct FusedParams {
   int kb_dn = 0;   // down k-blocks: ceil(I / 64)
   int lag = 1;     // L, in m-tiles
   int64_t H = 0, I = 0;
-  uint16_t* xs = nullptr;              // [rows_cap, H] gate_up input rows
   uint16_t* h = nullptr;               // [rows_cap, I]
   uint16_t* y = nullptr;               // [rows_cap, H] unless the output has seg_base
   unsigned int* claim = nullptr;       // tile claim counter, zero at launch
   unsigned int* h_ready = nullptr;     // per m-tile: gate_up epilogue warps done, zero at launch
-  unsigned int* y_ready = nullptr;     // per m-tile: down epilogue warps done, zero at launch
   int* err = nullptr;
 };
 
@@ -191,80 +189,16 @@ __device__ void dispatch_chunk(const GemmDispatch& D, int64_t c, int lane) {
   if (n_run) dispatch_flush(D, e_run, n_run, lane);
 }
 
-// Return: rows [32 q, 32 q + 32) of m-tile mt (a segment of another rank) of down-GEMM output,
-// staged in place of the m-tile's input rows, stored into the source rank's buffer.
-__device__ void return_quarter(const FusedParams& P, const GemmOutput& tgt,
-                               const int32_t* prefix, int32_t mt, int q, int lane) {
-  const int s = find_segment(prefix, P.nseg, mt);
-  const int32_t row0 = P.seg_offsets[s] + (mt - prefix[s]) * 128 + 32 * q;
-  const int32_t end = P.seg_offsets[s + 1] < P.rows_cap ? P.seg_offsets[s + 1] : P.rows_cap;
-  const int nr = end - row0 < 32 ? end - row0 : 32;
-  const int64_t vpr = P.H / 8;
-  const uint64_t base = tgt.seg_base[s];
-  for (int r = 0; r < nr; r += 2) {
-    const bool two = r + 1 < nr;
-    const int64_t ra = row0 + r, rb = row0 + (two ? r + 1 : r);
-    copy_row_pair(reinterpret_cast<const uint4*>(P.xs + ra * P.H),
-                  reinterpret_cast<uint4*>(
-                      base + static_cast<uint64_t>((ra - P.seg_offsets[s]) * P.H * 2)),
-                  reinterpret_cast<const uint4*>(P.xs + rb * P.H),
-                  reinterpret_cast<uint4*>(
-                      base + static_cast<uint64_t>((rb - P.seg_offsets[s]) * P.H * 2)),
-                  two, vpr, lane);
-  }
-}
-
-// Copy-warp loop. Return items (32 rows each, in m-tile order) are dealt round-robin to the
-// grid's copy warps; a warp forwards its next item as soon as that m-tile's down tiles are
-// stored, and otherwise takes the next dispatch chunk from the shared counter. Each warp polls
-// only its own item's counter (with backoff), so no single address is hammered by every warp.
-__device__ void copy_warp_loop(const GemmDispatch& D, const FusedParams& P,
-                               const GemmOutput& tgt, const int32_t* prefix, int32_t M,
-                               volatile int* abort, int cw, int n_cw, int lane) {
+// Copy-warp loop: claim 16-row dispatch chunks until none are left.
+__device__ void copy_warp_loop(const GemmDispatch& D, int lane) {
   constexpr int kChunkRows = 16;
   const int64_t nchunks = (D.n_rows + kChunkRows - 1) / kChunkRows;
-  const int32_t m0 = prefix[D.El];   // m-tiles from here on hold rows of other ranks
-  const int64_t n_ret = static_cast<int64_t>(M - m0) * 4;
-  const uint32_t y_target = 4u * static_cast<uint32_t>(P.n_dn);
-  bool dispatch_left = nchunks > 0;
-  int64_t item = cw;
-  uint64_t idle_since = 0;
-  uint32_t backoff = 64;
   for (;;) {
-    if (item < n_ret) {
-      int ready = 0;
-      if (lane == 0)
-        ready = load_acquire_gpu(P.y_ready + m0 + static_cast<int32_t>(item / 4)) == y_target;
-      if (__shfl_sync(0xffffffffu, ready, 0)) {
-        return_quarter(P, tgt, prefix, m0 + static_cast<int32_t>(item / 4),
-                       static_cast<int>(item & 3), lane);
-        item += n_cw;
-        idle_since = 0;
-        backoff = 64;
-        continue;
-      }
-    }
-    if (dispatch_left) {
-      unsigned int claimed = 0;
-      if (lane == 0) claimed = atomicAdd(D.claim, 1u);
-      const int64_t c = __shfl_sync(0xffffffffu, claimed, 0);
-      if (c < nchunks) {
-        dispatch_chunk(D, c, lane);
-        idle_since = 0;
-        continue;
-      }
-      dispatch_left = false;
-    }
-    if (item >= n_ret) break;
-    // this warp's next return item is not stored yet: wait (bounded)
-    if (idle_since == 0) idle_since = global_timer_ns();
-    if (*abort || global_timer_ns() - idle_since > kPeerWaitNs) {
-      *abort = 1;
-      record_device_error(P.err, PRISM_MOE_ERR_TIMEOUT);
-      break;
-    }
-    __nanosleep(backoff);
-    if (backoff < 2048) backoff <<= 1;
+    unsigned int claimed = 0;
+    if (lane == 0) claimed = atomicAdd(D.claim, 1u);
+    const int64_t c = __shfl_sync(0xffffffffu, claimed, 0);
+    if (c >= nchunks) break;
+    dispatch_chunk(D, c, lane);
   }
 }
 
@@ -482,8 +416,7 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
     }
   } else if (kDispatch && warp >= 6) {
     // ------------------------------------------------------------------ copy warps
-    copy_warp_loop(disp, P, tgt, prefix, M, abort, static_cast<int>(blockIdx.x) * 4 + (warp - 6),
-                   static_cast<int>(gridDim.x) * 4, lane);
+    copy_warp_loop(disp, lane);
   } else if (warp >= 2) {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
@@ -530,23 +463,14 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
         __syncwarp();
         if (lane == 0) add_release_gpu(P.h_ready + tr.mt, 1u);
       } else {
-        // rows of another rank's segment are staged in place of the m-tile's input rows (all
-        // of its gate_up tiles are done) and forwarded by the copy warps
-        const bool staged = kDispatch && s >= disp.El;
         uint64_t my_ptr = 0;
         if (has_row)
-          my_ptr = staged ? reinterpret_cast<uint64_t>(P.xs + row * P.H)
-                   : tgt.seg_base
+          my_ptr = tgt.seg_base
                        ? tgt.seg_base[s] +
                              static_cast<uint64_t>((row - P.seg_offsets[s]) * P.H * 2)
                        : reinterpret_cast<uint64_t>(P.y + row * P.H);
         drain_tile<false>(taddr, my_ptr, stage_out, lane, static_cast<int64_t>(tr.nt) * kBN,
                           P.H);
-        if (staged) {
-          __threadfence();
-          __syncwarp();
-          if (lane == 0) add_release_gpu(P.y_ready + tr.mt, 1u);
-        }
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
@@ -594,9 +518,9 @@ int64_t max_mtiles(int64_t rows_cap) { return ceil_div(rows_cap, 128) + kMaxSegm
 
 }  // namespace
 
-// [0] tile claim, [1] unused, h_ready[max m-tiles], y_ready[max m-tiles]
+// [0] tile claim, [1] unused, h_ready[max m-tiles]
 size_t fused_sync_bytes(int64_t rows_cap) {
-  return sizeof(unsigned int) * static_cast<size_t>(2 + 2 * max_mtiles(rows_cap));
+  return sizeof(unsigned int) * static_cast<size_t>(2 + max_mtiles(rows_cap));
 }
 
 int expert_swiglu_fused(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
@@ -604,8 +528,6 @@ int expert_swiglu_fused(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
                         const void* wgu, const void* wd, void* y, void* h, unsigned int* sync,
                         int* err, cudaStream_t st, const GemmOutput* down_out,
                         const GemmDispatch* dispatch) {
-  PRISM_CHECK_ARG(!dispatch || (down_out && down_out->seg_base),
-                  "fused experts: a dispatching step needs per-segment return addresses");
   CUtensorMap maps[4];
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(H), static_cast<uint64_t>(rows_cap)};
@@ -654,12 +576,10 @@ int expert_swiglu_fused(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
   if (const char* lg = std::getenv("PRISM_MOE_FUSED_LAG")) P.lag = std::max(1, std::atoi(lg));
   P.H = H;
   P.I = I;
-  P.xs = static_cast<uint16_t*>(const_cast<void*>(xs));
   P.h = static_cast<uint16_t*>(h);
   P.y = static_cast<uint16_t*>(y);
   P.claim = sync;
   P.h_ready = sync + 2;
-  P.y_ready = sync + 2 + max_mtiles(rows_cap);
   P.err = err;
   PRISM_CUDA(cudaMemsetAsync(sync, 0, fused_sync_bytes(rows_cap), st));
   const GemmOutput dense{};

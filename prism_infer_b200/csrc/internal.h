@@ -27,8 +27,7 @@ struct GemmOutput {
 // to that receive segment's arrival counter on the owner. The receive layout on rank d is
 // segment (j, le), index j * El + le = rows of local expert le from source (d - j) mod W. The
 // GEMM's producer waits (bounded) until the arrival counter of the segment a tile reads equals
-// the segment's row count. The same copy warps later forward the down GEMM's output rows of
-// other ranks' segments to their sources (GemmOutput::seg_base).
+// the segment's row count.
 struct GemmDispatch {
   const void* x = nullptr;              // [T, H] this rank's token rows
   int64_t vpr = 0;                      // 16-byte vectors per row
@@ -73,7 +72,7 @@ inline unsigned int* fused_sync(void* scratch, int64_t rows_cap, int64_t I) {
 // expert_gemm_sm100.cu — records profiling stage slots 3, 4 (two-launch engines only), 5.
 // ``h`` is the scratch above. ``down_out`` (optional) redirects the down GEMM's rows (y may
 // then be NULL) and adds a completion signal. ``dispatch`` (optional) runs the expert-parallel
-// dispatch and return copies inside the fused launch.
+// dispatch inside the fused launch.
 int expert_swiglu_bf16(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
                        const int32_t* seg_offsets, const int32_t* seg_expert, int nseg, int El,
                        const void* wgu, const void* wd, void* y, void* h, int* err,
