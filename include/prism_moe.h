@@ -204,7 +204,8 @@ int prism_moe_ep_ipc_handle_bytes(void);
 int prism_moe_ep_open_peer(const void* ipc_handle, void** ptr);
 int prism_moe_ep_close_peer(void* ptr);
 
-/* Bytes of the per-rank workspace prism_moe_ep_forward needs. */
+/* Bytes of the per-rank workspace prism_moe_ep_forward needs. Zero-fill it once before the
+ * first step and pass the same workspace to every step (it carries completion counters). */
 size_t prism_moe_ep_workspace_size(int64_t max_tokens, int64_t hidden, int64_t inter,
                                    int32_t num_experts, int32_t top_k, int32_t ep_size, int dtype);
 
@@ -218,7 +219,10 @@ size_t prism_moe_ep_workspace_size(int64_t max_tokens, int64_t hidden, int64_t i
  *   w_gate_up [E/W, 2I, H], w_down [E/W, H, I]: this rank's experts e in [rank*E/W, (rank+1)*E/W)
  *   my_landing: this rank's landing zone; peer_landing: DEVICE array of W uint64 landing-zone
  *   addresses as mapped in this process (entry ep_rank = my_landing).
- * T <= max_tokens (the landing capacity).
+ * T <= max_tokens (the landing capacity). Kernels: route (when logits are given), dispatch plan,
+ * counts all-gather, one fused expert launch (both GEMMs; its copy warps write the rows into the
+ * owners' receive buffers, its down epilogue writes the outputs back into the sources' buffers),
+ * wait for the returned rows, combine.
  */
 int prism_moe_ep_forward(const void* x, const void* router_logits, const int64_t* topk_ids,
                          const void* topk_weights, int dtype, int64_t num_tokens,
@@ -231,8 +235,10 @@ int prism_moe_ep_forward(const void* x, const void* router_logits, const int64_t
 /*
  * Profiling hook: CUDA events (cudaEvent_t handles owned by the caller) that the following
  * calls on this thread record on their stream at stage boundaries — slot 0 route begin,
- * 1 dispatch-plan begin, 2 permute begin, 3 gate_up GEMM begin, 4 down GEMM begin, 5 combine
- * begin, 6 combine end (prism_moe_expert_swiglu records slots 3-5). ``count`` = 0 turns it off.
+ * 1 dispatch-plan begin, 2 permute begin (EP: counts all-gather begin), 3 gate_up GEMM begin,
+ * 4 down GEMM begin, 5 combine begin, 6 combine end (prism_moe_expert_swiglu records slots 3-5;
+ * when both GEMMs run as one fused launch — always under expert parallelism — slot 4 is
+ * recorded with slot 5, after the launch). ``count`` = 0 turns it off.
  * The reference has no equivalent (it times whole engine steps with host clocks,
  * prism_infer bench/bench.py:445-452); this exists so a benchmark can time each kernel on the
  * device inside its timed region.
