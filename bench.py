@@ -423,6 +423,20 @@ def run_ours(args):
                                 "weight_bytes_per_step": wbytes,
                                 "hbm_gbs": wbytes / t_step / 1e9,
                                 "frac_of_hbm_peak": wbytes / t_step / 1e9 / hbm_peak}
+        # the same step captured once in a CUDA graph and replayed (no host work per step)
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side), torch.inference_mode():
+            for _ in range(2):
+                moe(xd)
+        torch.cuda.current_stream(device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.inference_mode(), torch.cuda.graph(graph):
+            moe(xd)
+        ms_g = time_device(lambda _i: graph.replay(), 200, 20, 1)
+        extra["decode_cfg1"]["graph_ms_per_step"] = ms_g / 200
+        extra["decode_cfg1"]["graph_hbm_gbs"] = wbytes / (ms_g / 200 / 1e3) / 1e9
+        del graph
 
     # ---- CPU baseline (rank 0, N=1) ----
     cpu = None
