@@ -208,13 +208,27 @@ __global__ void __launch_bounds__(1024)
   __syncthreads();
   // 6. return address of each segment's first row: its source's back buffer, at the source's
   //    expert-major row of its first row for my expert le
-  for (int s = 0; s < W; ++s) {
-    const int32_t c = i < E ? C[s * E + i] : 0;
-    const int32_t ex_s = block_excl_scan(c, E, tmp, nullptr);
-    if (i < E && i / El == me) {
+  //    One warp per source rank scans that source's histogram 32 experts at a time.
+  {
+    const int lane = i & 31;
+    for (int s = i >> 5; s < W; s += blockDim.x >> 5) {
       const int j = (me - s + W) % W;
-      seg_base[j * El + (i - me * El)] =
-          peers[s] + back_off + static_cast<uint64_t>(ex_s) * static_cast<uint64_t>(row_bytes);
+      int32_t carry = 0;
+      for (int base = 0; base < (me + 1) * El; base += 32) {
+        const int e = base + lane;
+        const int32_t c = e < E ? C[s * E + e] : 0;
+        int32_t incl = c;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const int32_t y = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += y;
+        }
+        if (e >= me * El && e < (me + 1) * El)
+          seg_base[j * El + (e - me * El)] =
+              peers[s] + back_off +
+              static_cast<uint64_t>(carry + incl - c) * static_cast<uint64_t>(row_bytes);
+        carry += __shfl_sync(0xffffffffu, incl, 31);
+      }
     }
   }
   // 7. where this rank announces C (outputs landed) on each peer. The dispatch's chunk counter
