@@ -128,6 +128,14 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def workload_config(tokens_per_rank, world):
+    """The ``config`` of both arms' JSON lines (benchmark config 2 at EP=world)."""
+    return {"workload": "cfg2: Qwen3-30B-A3B MoE block H=2048 E=128 top-8 I=768",
+            "tokens_per_rank": tokens_per_rank, "global_batch": tokens_per_rank * world,
+            "ep": world, "parallelism": f"ep{world}",
+            "l2": "inputs larger than L2: 1.2 GB of expert weights streamed per step"}
+
+
 def launches_per_step(world, fused):
     """This library's kernels per MoE.forward (the router GEMM is torch's): route, plan (chunk,
     scan, scatter), then EP=1: permute, experts (2 launches, or 1 fused), combine; EP>1: counts
@@ -239,7 +247,8 @@ def run_reference(args):
     H, E, k, I = CFG["H"], CFG["E"], CFG["k"], CFG["I"]
     wts = synthetic.make_weights_np(H, E, I, 2000)
     x = synthetic.make_hidden_np(sample, H, 2000)
-    O.moe_forward(x, wts.w_gate, wts.w_gate_up, wts.w_down, k, True, "float32")   # warm-up
+    for _ in range(max(1, min(args.warmup, 3))):                                   # warm-up
+        O.moe_forward(x, wts.w_gate, wts.w_gate_up, wts.w_down, k, True, "float32")
     t0 = time.perf_counter()
     for _ in range(args.steps):
         O.moe_forward(x, wts.w_gate, wts.w_gate_up, wts.w_down, k, True, "float32")
@@ -252,8 +261,8 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "cfg2 block H=2048 E=128 k=8 I=768 (CPU sample)",
-                   "sample_tokens_per_step": sample, "parallelism": "cpu"},
+        "config": {**workload_config(args.tokens, args.gpus),
+                   "sample_tokens_per_step": sample},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": desc},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -452,10 +461,7 @@ def run_ours(args):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
         "warmup": warmup, "ms_per_step": ms / steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "cfg2: Qwen3-30B-A3B MoE block H=2048 E=128 top-8 I=768",
-                   "tokens_per_rank": T, "global_batch": T * world, "ep": world,
-                   "parallelism": f"ep{world}",
-                   "l2": "inputs larger than L2: 1.2 GB of expert weights streamed per step"},
+        "config": workload_config(T, world),
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * H * 2,
