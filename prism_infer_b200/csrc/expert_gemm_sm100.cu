@@ -401,14 +401,18 @@ enum class Engine { kFused, kSingle, kPair };
 // Pair tiles (256 rows) pay off once segments are long: tail tiles waste up to 255 rows per
 // segment, single tiles up to 127. A dispatching step runs both GEMMs as one fused launch
 // (expert_fused_sm100.cu), so that the dispatch and the down GEMM's stores into peers overlap
-// tensor-core work. PRISM_MOE_GEMM_ENGINE=fused|single|pair overrides the choice for steps
-// without a dispatch (single = two launches with 128-row tiles).
+// tensor-core work; so does a step whose segments average under one m-tile (decode: the
+// launch boundary between the GEMMs would idle the GPU while each weight stream runs once,
+// measured 7% slower at 64 tokens). PRISM_MOE_GEMM_ENGINE=fused|single|pair overrides the
+// choice for steps without a dispatch (single = two launches with 128-row tiles).
 Engine pick_engine(int64_t rows_cap, int nseg, bool dispatch) {
   const char* force = std::getenv("PRISM_MOE_GEMM_ENGINE");
   if (dispatch || (force && force[0] == 'f')) return Engine::kFused;
   if (force && force[0] == 's') return Engine::kSingle;
   if (force && force[0] == 'p') return Engine::kPair;
-  return rows_cap / std::max(nseg, 1) >= 2048 ? Engine::kPair : Engine::kSingle;
+  const int64_t per_seg = rows_cap / std::max(nseg, 1);
+  if (per_seg < 128) return Engine::kFused;
+  return per_seg >= 2048 ? Engine::kPair : Engine::kSingle;
 }
 
 }  // namespace
