@@ -11,7 +11,14 @@ prism_infer/engine/parallel/expert_parallel.py, on B200 kernels.
 * ``ExpertParallelMoE`` — experts sharded by rank, tokens exchanged with all-to-all
   (expert_parallel.py:91-176).
 
-Exchange layout. The reference sends rows in perm order (grouped by destination rank, flat
+Transports. ``p2p`` (the default for bf16 on CUDA) runs the whole step in the library's
+``prism_moe_ep_forward``: a device-side counts all-gather, then one fused expert launch whose
+copy warps write the rows into the owners' CUDA-IPC-mapped receive buffers and whose down
+epilogue writes the outputs back into the sources' buffers — no host synchronisation. ``nccl``
+keeps the reference's structure (all_to_all_single with a host read of the split sizes) around
+the library's kernels, with the layout below.
+
+Exchange layout (nccl). The reference sends rows in perm order (grouped by destination rank, flat
 order inside) and the receiver regroups them per local expert with boolean masks
 (:165-169). Here rows are sent in expert-major order — destination rank, then local expert, then
 flat order — which is the same rank grouping refined by expert (experts are owned in contiguous
