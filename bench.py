@@ -12,14 +12,26 @@ Reported:
 * ``value``: tokens/s over all ranks, device-timed (CUDA events, barrier + synchronize on both
   sides, max over ranks), inputs resident in HBM;
 * ``e2e``: the same metric through ``MoE.forward`` with the step's hidden states copied from
-  pinned host memory and the output copied back inside the timed region;
-* ``roofline``: the grouped gate_up GEMM (the dominant kernel), its algorithmic FLOPs per
-  launch over its average event-timed duration, against the measured bf16 peak;
-* ``cpu_baseline``: the numpy oracle (a restatement of the reference's CPU path) on a bounded
-  sample of the same workload, on the host's cores (rank 0, N=1 only);
-* ``decode_cfg1``: config 1 (T=64, single GPU) at N=1, HBM roofline.
-``--impl reference`` times the reference algorithm on the host CPU (the oracle port), rank 0
-only, on a sample of the same workload per step.
+  pinned host memory and the output copied back inside the timed region, next to the same
+  copies timed alone (``copy_only``);
+* ``roofline``: the dominant kernel (N=1: the grouped gate_up GEMM; N>1: the fused expert launch
+  with the exchange inside), its algorithmic FLOPs per launch over its average event-timed
+  duration, against the measured bf16 peak;
+* ``parity``: after timing, on every rank — routing of every token compared bit for bit with
+  torch's own CUDA softmax / top-k / renorm on the same logits (the reference's calls,
+  prism_infer/layers/moe.py:74-81), the device error word, and sampled tokens' outputs against
+  the reference's expert math run with torch ops (bf16 F.linear, SiluAndMul with one rounding,
+  combine_weighted_sum) on the same routing;
+* ``cfg3`` / ``cfg4``: benchmark configs 3 (Zipf-skewed routing, T=4096/rank) and 4
+  (Qwen3-235B-A22B block, H=4096, I=1536, T=16384/rank) at the same EP size, each with its own
+  parity; ``decode_cfg1``: config 1 (T=64, single GPU) at N=1, HBM roofline;
+* ``a2a`` (N>1): NVLink bytes each rank sends per step, the dispatch window stamped inside the
+  fused launch (%globaltimer) and the bandwidths they give;
+* ``cpu_baseline``: the numpy restatement of the reference's CPU path on a bounded sample of the
+  same workload, on the host's cores (rank 0, N=1 only).
+``--impl reference`` times the reference algorithm on the host CPU (the numpy port; the
+reference is Python over torch with no native code to build), rank 0 only, one full per-rank
+batch (T=8192 tokens) per step, on every host thread it may use.
 """
 from __future__ import annotations
 
@@ -38,8 +50,17 @@ sys.path.insert(0, str(REPO))
 
 METRIC = "MoE-block tokens/s (Qwen3-30B-A3B block, EP=N, T=8192/rank)"
 UNIT = "tokens/s"
-CFG = dict(T=8192, H=2048, E=128, k=8, I=768)
+CFGS = {
+    2: dict(T=8192, H=2048, E=128, k=8, I=768, skew=False,
+            name="cfg2: Qwen3-30B-A3B MoE block H=2048 E=128 top-8 I=768"),
+    3: dict(T=4096, H=2048, E=128, k=8, I=768, skew=True,
+            name="cfg3: cfg2 block, Zipf(1.2)-skewed routing, top expert ~8x mean load"),
+    4: dict(T=16384, H=4096, E=128, k=8, I=1536, skew=False,
+            name="cfg4: Qwen3-235B-A22B MoE block H=4096 E=128 top-8 I=1536"),
+}
+CFG = CFGS[2]
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+PARITY_MAX_ABS, PARITY_MEAN_REL = 2e-2, 1e-2     # bf16 tolerance of the north star
 
 
 def parse_args():
@@ -51,6 +72,7 @@ def parse_args():
     ap.add_argument("--tokens", type=int, default=CFG["T"], help="tokens per rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-extra-configs", action="store_true")
     return ap.parse_args()
 
 
@@ -130,7 +152,7 @@ class ClockSampler:
 
 def workload_config(tokens_per_rank, world):
     """The ``config`` of both arms' JSON lines (benchmark config 2 at EP=world)."""
-    return {"workload": "cfg2: Qwen3-30B-A3B MoE block H=2048 E=128 top-8 I=768",
+    return {"workload": CFG["name"],
             "tokens_per_rank": tokens_per_rank, "global_batch": tokens_per_rank * world,
             "ep": world, "parallelism": f"ep{world}",
             "l2": "inputs larger than L2: 1.2 GB of expert weights streamed per step"}
@@ -162,17 +184,21 @@ def dist_setup(n):
     return rank, world, local
 
 
-def build_block(T, world, rank, device, cfg_id=2):
+def build_block(cfg_id, T, world, rank, device):
+    """The drop-in ``MoE`` of benchmark config ``cfg_id`` with this rank's experts, and this
+    rank's hidden states (seeded per config and rank)."""
     import torch
 
     from prism_infer_b200 import synthetic
     from prism_infer_b200.engine.parallel import set_expert_parallel_size
     from prism_infer_b200.layers.moe import MoE
-    H, E, k, I = CFG["H"], CFG["E"], CFG["k"], CFG["I"]
+    c = CFGS[cfg_id]
+    H, E, k, I = c["H"], c["E"], c["k"], c["I"]
     seed = synthetic.config_seed(cfg_id)
     set_expert_parallel_size(world)
     El = E // world
     wg, wgu, wd = synthetic.make_weights_torch(H, E, I, seed, torch.bfloat16, device,
+                                               skew=c["skew"], k=k,
                                                expert_range=(rank * El, (rank + 1) * El))
     moe = MoE(H, I, E, k).to(device=device, dtype=torch.bfloat16)
     bank = moe.ep_moe if world > 1 else moe
@@ -181,8 +207,16 @@ def build_block(T, world, rank, device, cfg_id=2):
         bank.w_gate_up.copy_(wgu)
         bank.w_down.copy_(wd)
     x = synthetic.make_hidden_torch(T, H, synthetic.config_seed(cfg_id, rank), torch.bfloat16,
-                                    device)
+                                    device, skew=c["skew"])
     return moe, x
+
+
+def free_block(moe, world):
+    import torch
+    if world > 1 and moe.ep_moe is not None:
+        moe.ep_moe.release()          # collective
+    del moe
+    torch.cuda.empty_cache()
 
 
 def time_device(fn, steps, warmup, world, nvtx=None):
@@ -216,11 +250,148 @@ def time_device(fn, steps, warmup, world, nvtx=None):
     return ms
 
 
+def reduce_over_ranks(vals, op, world):
+    """Elementwise reduction of a list of floats over the ranks (op: "max", "min", "sum")."""
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return list(vals)
+    t = torch.tensor(vals, dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op={"max": dist.ReduceOp.MAX, "min": dist.ReduceOp.MIN,
+                           "sum": dist.ReduceOp.SUM}[op])
+    return t.tolist()
+
+
+def check_device_error(moe, world, device):
+    """Status of the block's device error word after the timed steps (0 = none)."""
+    try:
+        if world > 1:
+            moe.ep_moe.check_device_error()
+        else:
+            moe.check_device_error(device)
+        return 0
+    except RuntimeError as e:
+        msg = str(e)
+        return int(msg.split("status ")[1].split(":")[0]) if "status " in msg else -1
+
+
+def parity_check(moe, x, cfg_id, world, rank, device, n_sample=32):
+    """Parity of one more step of ``moe`` on ``x`` (see the module docstring). Routing is checked
+    for every token; outputs for ``n_sample`` tokens spread over the batch, against the reference's
+    expert arithmetic on the same routing (a token's output depends only on its own row). Remote
+    experts' weights are regenerated from their seeds. Returns the rank-reduced summary."""
+    import torch
+    import torch.nn.functional as F
+
+    from prism_infer_b200 import capi, synthetic
+    c = CFGS[cfg_id]
+    H, E, k, I = c["H"], c["E"], c["k"], c["I"]
+    T = x.shape[0]
+    with torch.inference_mode():
+        logits = moe.gate(x)
+        out = moe(x)
+        ids, w, _ = capi.route_topk(logits.contiguous(), k, True)
+        # the reference's routing, moe.py:77-81, with torch's CUDA kernels
+        p = F.softmax(logits, dim=-1, dtype=torch.float)
+        rw, rid = torch.topk(p, k, dim=-1)
+        rw = (rw / rw.sum(dim=-1, keepdim=True)).to(x.dtype)
+        ids_mismatch = int((ids != rid).any(dim=-1).sum().item())
+        w_mismatch = int((w != rw).any(dim=-1).sum().item())
+        counts = torch.bincount(ids.reshape(-1), minlength=E)
+        sample = torch.linspace(0, T - 1, n_sample, device=device).round().long().unique()
+        xs, sid, sw = x[sample], rid[sample], rw[sample]
+        seed = synthetic.config_seed(cfg_id)
+        ys = torch.empty(sample.numel(), k, H, dtype=x.dtype, device=device)
+        for e in torch.unique(sid).tolist():
+            wgu, wd = synthetic.expert_weights_torch(H, I, seed, e, torch.bfloat16, device)
+            tt, jj = torch.nonzero(sid == e, as_tuple=True)
+            gu = F.linear(xs[tt], wgu)                                       # bf16, like cuBLAS
+            act = (F.silu(gu[:, :I].float()) * gu[:, I:].float()).to(x.dtype)   # compiled: 1 rounding
+            ys[tt, jj] = F.linear(act, wd)
+        ref = (ys * sw.unsqueeze(-1)).sum(dim=1)              # combine_weighted_sum (:45-57)
+        got = out[sample]
+        d = (got.float() - ref.float()).abs()
+        max_abs = float(d.max().item()) if d.numel() else 0.0
+        rel_num = float(d.sum().item())
+        rel_den = float(ref.float().abs().sum().item())
+    status = check_device_error(moe, world, device)
+    vals = reduce_over_ranks([ids_mismatch, w_mismatch, max_abs, rel_num, rel_den,
+                              float(status != 0), float(T)], "sum", world)
+    mx = reduce_over_ranks([max_abs, float(counts.max().item())], "max", world)
+    load = reduce_over_ranks(counts.float().tolist(), "sum", world)
+    mean_load = sum(load) / E
+    res = {
+        "ids_exact": vals[0] == 0, "weights_exact": vals[1] == 0,
+        "tokens_routed_checked": int(vals[6]), "tokens_with_different_ids": int(vals[0]),
+        "sampled_tokens_per_rank": int(sample.numel()), "max_abs": mx[0],
+        "mean_rel": vals[3] / max(vals[4], 1e-30), "device_error_ranks": int(vals[5]),
+        "tolerance": {"max_abs": PARITY_MAX_ABS, "mean_rel": PARITY_MEAN_REL},
+        "max_expert_load_over_mean": max(load) / mean_load if mean_load else None,
+    }
+    res["ok"] = bool(res["ids_exact"] and res["weights_exact"] and res["device_error_ranks"] == 0
+                     and res["max_abs"] <= PARITY_MAX_ABS
+                     and res["mean_rel"] <= PARITY_MEAN_REL)
+    return res
+
+
+def a2a_stats(moe, x, world, reps=5):
+    """NVLink exchange of an EP step from the in-kernel stamps (``prism_moe_ep_read_stats``),
+    averaged over ``reps`` steps; per-rank figures averaged over the ranks."""
+    import torch
+    H = x.shape[1]
+    acc = [0.0] * 5
+    for _ in range(reps):
+        with torch.inference_mode():
+            moe(x)
+        st = moe.ep_moe.step_stats()
+        disp_ns = max(st["dispatch_t1_ns"] - st["dispatch_t0_ns"], 1)
+        fused_ns = max(st["fused_t1_ns"] - st["fused_t0_ns"], 1)
+        sb, rb = st["send_rows"] * H * 2, st["recv_rows"] * H * 2
+        acc = [a + b for a, b in zip(acc, [sb, rb, disp_ns, fused_ns,
+                                           (sb + rb) / fused_ns])]
+    acc = [a / reps for a in acc]
+    tot = reduce_over_ranks(acc, "sum", world)
+    mean = [t / world for t in tot]
+    return {
+        "dispatch_remote_bytes_per_rank": mean[0],
+        "return_remote_bytes_per_rank": mean[1],
+        "dispatch_ms": mean[2] / 1e6,
+        "fused_launch_ms": mean[3] / 1e6,
+        "dispatch_gbs": mean[0] / mean[2],
+        "nvlink_out_gbs_over_fused_launch": mean[4],
+        "landing_zone_bytes_per_rank": moe.ep_moe.landing_bytes(),
+        "how": "per rank: rows sent to / returned to other ranks x H x 2 B; dispatch window = "
+               "first chunk claimed to last chunk stored (%globaltimer in the copy warps); "
+               "mean over ranks and 5 steps",
+    }
+
+
+def sub_config(cfg_id, world, rank, device, peak, steps=10, warmup=3):
+    """Throughput and parity of benchmark config ``cfg_id`` at EP=world."""
+    c = CFGS[cfg_id]
+    moe, x = build_block(cfg_id, c["T"], world, rank, device)
+    import torch
+
+    def step(_i):
+        with torch.inference_mode():
+            moe(x)
+    ms = time_device(step, steps, warmup, world)
+    t = ms / steps / 1e3
+    flops = c["T"] * (2 * c["H"] * c["E"] + c["k"] * 6 * c["H"] * c["I"])
+    res = {"workload": c["name"], "tokens_per_rank": c["T"], "ep": world, "steps": steps,
+           "ms_per_step": ms / steps, "tokens_per_s": world * c["T"] / t,
+           "block_tflops_per_gpu": flops / t / 1e12,
+           "block_frac_of_peak": flops / t / 1e12 / peak}
+    res["parity"] = parity_check(moe, x, cfg_id, world, rank, device, n_sample=16)
+    if world > 1:
+        res["a2a"] = a2a_stats(moe, x, world, reps=3)
+    free_block(moe, world)
+    return res
+
+
 def cpu_oracle_rate(sample_tokens, reps, seed=2000):
     """Tokens/s of the numpy oracle (fp32 restatement of the reference's MoE.forward) on
     ``sample_tokens`` tokens of the workload, best of ``reps``."""
-    import numpy as np
-
     from oracle import moe_oracle as O
     from prism_infer_b200 import synthetic
     H, E, k, I = CFG["H"], CFG["E"], CFG["k"], CFG["I"]
@@ -231,39 +402,50 @@ def cpu_oracle_rate(sample_tokens, reps, seed=2000):
         t0 = time.perf_counter()
         O.moe_forward(x, wts.w_gate, wts.w_gate_up, wts.w_down, k, True, "float32")
         best = min(best, time.perf_counter() - t0)
-    del np
     return sample_tokens / best, best
 
 
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def run_reference(args):
+    """The reference's block on the host CPU: the numpy port of MoE.forward (fp32), one full
+    per-rank batch per step, on every host thread this process may use. A launcher (torchrun)
+    sets OMP_NUM_THREADS=1 before Python starts, so the BLAS pool is resized explicitly."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    cores = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
-    sample = 256
+    cores = host_threads()
+    from threadpoolctl import threadpool_info, threadpool_limits
+
     from oracle import moe_oracle as O
     from prism_infer_b200 import synthetic
     H, E, k, I = CFG["H"], CFG["E"], CFG["k"], CFG["I"]
+    T = args.tokens
     wts = synthetic.make_weights_np(H, E, I, 2000)
-    x = synthetic.make_hidden_np(sample, H, 2000)
-    for _ in range(max(1, min(args.warmup, 3))):                                   # warm-up
-        O.moe_forward(x, wts.w_gate, wts.w_gate_up, wts.w_down, k, True, "float32")
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        O.moe_forward(x, wts.w_gate, wts.w_gate_up, wts.w_down, k, True, "float32")
-    dt = time.perf_counter() - t0
-    value = sample * args.steps / dt
-    desc = (f"numpy oracle (fp32 restatement of prism_infer MoE.forward, moe.py:69-100) on "
-            f"{sample} tokens of the workload per step, {cores} host threads")
+    x = synthetic.make_hidden_np(T, H, 2000)
+    with threadpool_limits(limits=cores):
+        used = max([d.get("num_threads", 1) for d in threadpool_info()] or [1])
+        for _ in range(max(1, min(args.warmup, 2))):                             # warm-up
+            O.moe_forward(x, wts.w_gate, wts.w_gate_up, wts.w_down, k, True, "float32")
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            O.moe_forward(x, wts.w_gate, wts.w_gate_up, wts.w_down, k, True, "float32")
+        dt = time.perf_counter() - t0
+    value = T * args.steps / dt
+    desc = (f"numpy port of prism_infer MoE.forward (moe.py:69-100), fp32, {T} tokens "
+            f"(one rank's full batch) per step, BLAS on {used} of {cores} host threads")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {**workload_config(args.tokens, args.gpus),
-                   "sample_tokens_per_step": sample},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+        "config": {**workload_config(T, args.gpus), "sample_tokens_per_step": T},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": used, "kind": "port",
                          "sample": desc},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -279,8 +461,10 @@ def run_ours(args):
     device = torch.device("cuda", local)
     T = args.tokens
     H, E, k, I = CFG["H"], CFG["E"], CFG["k"], CFG["I"]
-    moe, x = build_block(T, world, rank, device)
+    moe, x = build_block(2, T, world, rank, device)
     peaks, peak_kind = load_peaks()
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
 
     # ---- device-resident timing with per-stage events ----
     steps, warmup = args.steps, args.warmup
@@ -307,7 +491,7 @@ def run_ours(args):
     gpu_ids = ([int(v) for v in vis.split(",")][:world] if vis and all(
         v.strip().isdigit() for v in vis.split(",")) else list(range(world)))
     clocks = sampler.stop(gpu_ids) if sampler else None
-    moe.check_device_error(device) if world == 1 else None
+    status_after_timing = check_device_error(moe, world, device)
 
     # per-stage averages (ms) — slots: route, plan, permute, gate_up, down, combine
     # EP>1: "exchange" is the counts all-gather; the row dispatch and return run inside the
@@ -330,6 +514,12 @@ def run_ours(args):
         stage_ms.pop("down")
     value = world * T * steps / (ms / 1e3)
 
+    # ---- parity of the timed configuration, on every rank ----
+    parity = parity_check(moe, x, 2, world, rank, device)
+    parity["device_error_after_timing"] = int(reduce_over_ranks(
+        [float(status_after_timing != 0)], "sum", world)[0])
+    parity["ok"] = parity["ok"] and parity["device_error_after_timing"] == 0
+
     # ---- end to end through MoE.forward with host buffers ----
     # Every step copies its hidden states from pinned host memory and its output back. The
     # copies run on their own streams, double-buffered, so step i+1's upload and step i-1's
@@ -337,6 +527,7 @@ def run_ours(args):
     x_host = [x.detach().cpu().pin_memory() for _ in range(2)]
     y_host = [torch.empty_like(x_host[0]).pin_memory() for _ in range(2)]
     x_dev = [torch.empty_like(x) for _ in range(2)]
+    y_dev = [torch.empty_like(x) for _ in range(2)]
     s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
     comp = torch.cuda.current_stream(device)
     ev_in = [torch.cuda.Event() for _ in range(2)]
@@ -345,33 +536,37 @@ def run_ours(args):
     for e in ev_done + ev_out:
         e.record(comp)
 
-    def e2e_step(i):
+    def e2e_step(i, forward=True):
         b = i % 2
         s_in.wait_event(ev_done[b])          # x_dev[b] no longer read by step i-2
         with torch.cuda.stream(s_in):
             x_dev[b].copy_(x_host[b], non_blocking=True)
             ev_in[b].record(s_in)
         comp.wait_event(ev_in[b])
-        with torch.inference_mode():
-            y = moe(x_dev[b])
+        if forward:
+            with torch.inference_mode():
+                y = moe(x_dev[b])
+        else:
+            y = y_dev[b]
         ev_done[b].record(comp)
         s_out.wait_event(ev_done[b])
         s_out.wait_event(ev_out[b])          # y_host[b] free (step i-2's copy finished)
         with torch.cuda.stream(s_out):
             y_host[b].copy_(y, non_blocking=True)
-            y.record_stream(s_out)
+            if forward:
+                y.record_stream(s_out)
             ev_out[b].record(s_out)
 
-    def e2e_loop_end():
-        comp.wait_stream(s_out)
+    def e2e_timed(forward):
+        def fn(i):
+            e2e_step(i, forward)
+            if i == steps - 1 or i < 0:
+                comp.wait_stream(s_out)
+        return fn
 
-    def e2e_step_timed(i):
-        e2e_step(i)
-        if i == steps - 1 or i < 0:
-            e2e_loop_end()
-
-    ms_e2e = time_device(e2e_step_timed, steps, max(2, warmup // 2), world)
+    ms_e2e = time_device(e2e_timed(True), steps, max(2, warmup // 2), world)
     e2e_value = world * T * steps / (ms_e2e / 1e3)
+    ms_copy = time_device(e2e_timed(False), steps, max(2, warmup // 2), world)
 
     # ---- roofline of the dominant kernel ----
     # fused engine (EP>1): both expert GEMMs in one launch, 6*H*I FLOP per routed row;
@@ -388,7 +583,6 @@ def run_ours(args):
         kname = "grouped_gemm_sm100_kernel<gate_up>"
         algo = f"2*{rows}*{H}*{2 * I} = {kflops:.4g} FLOP per launch"
     achieved = kflops / (kms / 1e3) / 1e12
-    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
     traffic = ncu_traffic("fused" if fused else "gate_up")
     roofline = {"bound": "tensor", "kernel": kname,
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
@@ -399,20 +593,21 @@ def run_ours(args):
         "stages_ms": stage_ms,
         "block_tflops": block_flops * steps / (ms / 1e3) / 1e12 / world,
         "block_frac_of_peak": block_flops * steps / (ms / 1e3) / 1e12 / world / peak,
+        "parity": parity,
     }
-    hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
     if world == 1:
         el = 2
         perm_bytes = T * H * el + rows * H * el + rows * 4
         comb_bytes = rows * H * el + T * H * el + rows * (4 + el)
         extra["hbm"] = {
-            # bf16 fuses the permutation into the gate_up GEMM's gather loads
             "permute_gbs": (perm_bytes / (stage_ms["permute"] / 1e3) / 1e9
                             if stage_ms["permute"] > 1e-3 else "fused into gate_up"),
             "combine_gbs": comb_bytes / (stage_ms["combine"] / 1e3) / 1e9,
             "route_gbs": (T * E * el + T * k * (8 + el)) / (stage_ms["route"] / 1e3) / 1e9,
             "peak_gbs": hbm_peak,
         }
+    else:
+        extra["a2a"] = a2a_stats(moe, x, world)
 
     # ---- config 1 decode (T=64) at N=1 ----
     if world == 1 and not args.no_decode:
@@ -447,15 +642,26 @@ def run_ours(args):
         extra["decode_cfg1"]["graph_hbm_gbs"] = wbytes / (ms_g / 200 / 1e3) / 1e9
         del graph
 
+    free_block(moe, world)
+    del x_dev, y_dev
+
+    # ---- benchmark configs 3 and 4 at the same EP size ----
+    if not args.no_extra_configs:
+        for cid in (3, 4):
+            extra[f"cfg{cid}"] = sub_config(cid, world, rank, device, peak)
+
     # ---- CPU baseline (rank 0, N=1) ----
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        cores = os.cpu_count() or 1
+        from threadpoolctl import threadpool_info, threadpool_limits
+        cores = host_threads()
         sample = 512
-        rate, best = cpu_oracle_rate(sample, 2)
-        cpu = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": f"numpy oracle, fp32, {sample} tokens of the workload, best of 2 "
-                         f"({best:.2f} s each), {cores} host threads"}
+        with threadpool_limits(limits=cores):
+            used = max([d.get("num_threads", 1) for d in threadpool_info()] or [1])
+            rate, best = cpu_oracle_rate(sample, 2)
+        cpu = {"value": rate, "unit": UNIT, "cores": used, "kind": "port",
+               "sample": f"numpy port of MoE.forward, fp32, {sample} tokens of the workload, "
+                         f"best of 2 ({best:.2f} s each), BLAS on {used} host threads"}
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
@@ -466,8 +672,11 @@ def run_ours(args):
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * H * 2,
                 "d2h_bytes_per_step": T * H * 2,
+                "copy_only_ms_per_step": ms_copy / steps,
+                "ms_per_step": ms_e2e / steps,
                 "how": "MoE.forward; per step H2D of x from pinned host and D2H of the output, "
-                       "on copy streams double-buffered against the forward"},
+                       "on copy streams double-buffered against the forward; copy_only: the "
+                       "same copies with no forward"},
         "gpu_launches": steps * launches_per_step(world, fused),
         "clocks": clocks,
         **extra,

@@ -39,6 +39,12 @@ extern "C" {
 #define PRISM_MOE_F32 0
 #define PRISM_MOE_BF16 1
 
+/* Expert GEMM engines (prism_moe_set_expert_engine). */
+#define PRISM_MOE_ENGINE_AUTO 0    /* chosen per call from the rows per segment (default)     */
+#define PRISM_MOE_ENGINE_FUSED 1   /* gate_up and down in one persistent launch, 128-row tiles */
+#define PRISM_MOE_ENGINE_SINGLE 2  /* two launches, 128-row tiles                              */
+#define PRISM_MOE_ENGINE_PAIR 3    /* two launches, 256-row tiles on CTA pairs (cta_group::2)  */
+
 /* Library version (major*10000 + minor*100 + patch). */
 int prism_moe_version(void);
 
@@ -82,7 +88,13 @@ size_t prism_moe_dispatch_workspace_size(int64_t num_tokens, int32_t top_k, int3
  *                                   flat order inside an expert); the layout the expert GEMMs
  *                                   and the EP send buffer use.
  * Requires num_experts % ep_size == 0 (the reference asserts the same,
- * expert_parallel.py:103).
+ * expert_parallel.py:103). Expert ids must lie in [0, num_experts): the reference fails on
+ * others (bincount of a negative destination, or an all_to_all split past the group). Here an
+ * entry with an id outside that range is left out of every output (entry_row = -1; its perm and
+ * sorted_local_eid slots, past the valid entries, are not written; the counts and splits do not
+ * include it) and the kernel records PRISM_MOE_ERR_ARG in the workspace's first int32 word,
+ * which prism_moe_read_device_error(workspace, stream) returns and clears. The workspace must
+ * start zeroed.
  */
 int prism_moe_build_dispatch_plan(const int64_t* topk_ids, int64_t num_tokens, int32_t top_k,
                                   int32_t num_experts, int32_t ep_size, int64_t* perm,
@@ -102,6 +114,9 @@ int prism_moe_build_dispatch_plan(const int64_t* topk_ids, int64_t num_tokens, i
  * return PRISM_MOE_ERR_ARG. The first call on a device looks up the array's address on that
  * device (make it before any stream capture starts). Calls share the array: calls whose
  * kernels may overlap on the GPU race and must be serialised. Allocates nothing.
+ * Expert ids must lie in [0, num_experts); entries outside it are left out of the outputs as
+ * in prism_moe_build_dispatch_plan, but the error word that records them lives in the shared
+ * array and is not reported to the caller.
  */
 int prism_moe_build_dispatch_plan_static(const int64_t* topk_ids, int64_t num_tokens,
                                          int32_t top_k, int32_t num_experts, int32_t ep_size,
@@ -213,7 +228,10 @@ size_t prism_moe_ep_workspace_size(int64_t max_tokens, int64_t hidden, int64_t i
  * One expert-parallel MoE block step on this rank (bf16). Replaces
  * prism_infer/layers/moe.py:77-85 + ExpertParallelMoE.forward
  * (prism_infer/engine/parallel/expert_parallel.py:140-176). Collective: every rank of the EP
- * group calls it once per step with the same ``epoch`` (1, 2, 3, ... increasing by one).
+ * group calls it once per step. ``epoch`` numbers the step: either 0 on every call (the library
+ * keeps the count in the workspace, so the arguments do not change from step to step and a
+ * step can be captured in a CUDA graph and replayed; every rank must then make the same number
+ * of calls) or the caller's count (1, 2, 3, ... increasing by one, the same on all ranks).
  *   x [T, H], out [T, H]; either router_logits [T, E] (routed here as prism_moe_route_topk) or
  *   topk_ids [T, k] int64 + topk_weights [T, k].
  *   w_gate_up [E/W, 2I, H], w_down [E/W, H, I]: this rank's experts e in [rank*E/W, (rank+1)*E/W)
@@ -223,6 +241,10 @@ size_t prism_moe_ep_workspace_size(int64_t max_tokens, int64_t hidden, int64_t i
  * counts all-gather, one fused expert launch (both GEMMs; its copy warps write the rows into the
  * owners' receive buffers, its down epilogue writes the outputs back into the sources' buffers),
  * wait for the returned rows, combine.
+ * Caller-given topk_ids outside [0, num_experts) are not sent anywhere (their slots add nothing
+ * to ``out``) and record PRISM_MOE_ERR_ARG in the workspace's error word. When a wait for other
+ * ranks runs out, PRISM_MOE_ERR_TIMEOUT is recorded there, the rest of that step does nothing
+ * and ``out`` is undefined; the group should then be torn down.
  */
 int prism_moe_ep_forward(const void* x, const void* router_logits, const int64_t* topk_ids,
                          const void* topk_weights, int dtype, int64_t num_tokens,
@@ -231,6 +253,29 @@ int prism_moe_ep_forward(const void* x, const void* router_logits, const int64_t
                          const void* w_gate_up, const void* w_down, void* my_landing,
                          const uint64_t* peer_landing, uint64_t epoch, void* out,
                          void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Statistics of the last prism_moe_ep_forward step that used ``workspace`` (synchronises
+ * ``stream``). ``stats`` receives 8 uint64 values: [0] the step's epoch, [1] the workspace's
+ * epoch counter, [2] and [3] %globaltimer ns when the first dispatch chunk was claimed and when
+ * the last one was stored, [4] and [5] when the fused expert launch's first CTA started and its
+ * last CTA finished, [6] rows sent to other ranks, [7] rows received from other ranks (each is
+ * returned to its source after the down GEMM). Row bytes = hidden * 2. The reference has no
+ * equivalent; this feeds the all-to-all bandwidth a benchmark reports.
+ */
+int prism_moe_ep_read_stats(const void* workspace, uint64_t* stats, void* stream);
+
+/*
+ * Process-wide controls, for tests and tuning (the defaults need no call).
+ * prism_moe_set_expert_engine: the expert GEMM engine for calls without an expert-parallel
+ * exchange (PRISM_MOE_ENGINE_*; AUTO picks by rows per segment; expert-parallel steps always use
+ * the fused launch). prism_moe_set_wait_limits: the bound, in ns, of every in-kernel wait on this
+ * GPU's own pipeline (default 2 s) and of every wait for other ranks (default 10 s); 0 restores a
+ * default, values above 60 s are rejected. The limits are read when a kernel is launched.
+ * Neither has a counterpart in the reference.
+ */
+int prism_moe_set_expert_engine(int engine);
+int prism_moe_set_wait_limits(int64_t wait_ns, int64_t peer_wait_ns);
 
 /*
  * Profiling hook: CUDA events (cudaEvent_t handles owned by the caller) that the following

@@ -19,6 +19,9 @@ HEADER = Path(__file__).resolve().parent.parent / "include" / "prism_moe.h"
 
 OK, ERR_ARG, ERR_CUDA, ERR_TIMEOUT, ERR_UNSUPPORTED, ERR_DEVICE = range(6)
 F32, BF16 = 0, 1
+ENGINES = {"auto": 0, "fused": 1, "single": 2, "pair": 3}
+EP_STATS_FIELDS = ("epoch", "counter", "dispatch_t0_ns", "dispatch_t1_ns", "fused_t0_ns",
+                   "fused_t1_ns", "send_rows", "recv_rows")
 
 _vp, _i32, _i64, _sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t
 _SIGNATURES = {
@@ -52,6 +55,9 @@ _SIGNATURES = {
     "prism_moe_ep_forward": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, _i64, _i64, _i64,
                                             _i64, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp,
                                             _vp, ctypes.c_uint64, _vp, _vp, _sz, _vp]),
+    "prism_moe_ep_read_stats": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_uint64), _vp]),
+    "prism_moe_set_expert_engine": (ctypes.c_int, [ctypes.c_int]),
+    "prism_moe_set_wait_limits": (ctypes.c_int, [_i64, _i64]),
     "prism_moe_profile_events": (ctypes.c_int, [ctypes.POINTER(_vp), _i32]),
     "prism_moe_read_device_error": (ctypes.c_int, [_vp, _vp]),
 }
@@ -223,6 +229,60 @@ def combine(expert_out, topk_weights, entry_row=None, out=None):
     return out
 
 
+_ws_lock = threading.Lock()
+_workspaces: dict = {}
+
+
+def block_workspace(device, nbytes: int):
+    """Per-(device, stream) scratch for ``prism_moe_block_forward``; grows on demand. The first
+    four bytes are the kernels' device error word (kept zero)."""
+    torch = _torch()
+    stream = torch.cuda.current_stream(device).cuda_stream
+    key = (device.index, stream)
+    with _ws_lock:
+        ws = _workspaces.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+            _workspaces[key] = ws
+    return ws
+
+
+def block_error_word(device):
+    """The device error word of the current stream's block workspace (None before any call)."""
+    torch = _torch()
+    ws = _workspaces.get((device.index, torch.cuda.current_stream(device).cuda_stream))
+    return None if ws is None else ws[:4].view(torch.int32)
+
+
+def block_forward(x, router_logits, w_gate_up, w_down, top_k: int, renorm: bool, out=None):
+    """The single-GPU block after the router GEMM (prism_moe_block_forward): route, plan,
+    gather, grouped SwiGLU experts, combine. ``x`` [T,H], ``router_logits`` [T,E],
+    ``w_gate_up`` [E,2I,H], ``w_down`` [E,H,I]; returns [T,H]."""
+    torch = _torch()
+    _need_cuda(x, router_logits, w_gate_up, w_down)
+    T, H = x.shape
+    E, twoI, H2 = w_gate_up.shape
+    I = twoI // 2
+    if H2 != H or tuple(w_down.shape) != (E, H, I) or tuple(router_logits.shape) != (T, E):
+        raise RuntimeError("block_forward: inconsistent shapes")
+    for t in (router_logits, w_gate_up, w_down):
+        if t.dtype != x.dtype:
+            raise RuntimeError(f"block_forward: dtype {t.dtype} != hidden dtype {x.dtype}")
+    if out is None:
+        out = torch.empty_like(x)
+    if T == 0:
+        return out
+    lib = load()
+    dt = dtype_code(x.dtype)
+    nbytes = lib.prism_moe_block_workspace_size(T, H, I, E, top_k, dt)
+    ws = block_workspace(x.device, nbytes)
+    check(lib.prism_moe_block_forward(
+        ptr(x), ptr(router_logits), dt, T, H, I, E, top_k, int(bool(renorm)), ptr(w_gate_up),
+        ptr(w_down), ptr(out), None, None, ptr(ws), ws.numel(), stream_of(x.device)),
+        "prism_moe_block_forward")
+    return out
+
+
 def ep_alloc_landing(nbytes: int):
     """Allocate this rank's landing zone; returns (device address, IPC handle bytes)."""
     lib = load()
@@ -254,3 +314,26 @@ def read_device_error(word, device=None) -> int:
     """Synchronise and return (and clear) the status in a device error word."""
     dev = word.device if device is None else device
     return load().prism_moe_read_device_error(ptr(word), stream_of(dev))
+
+
+def set_expert_engine(name: str) -> None:
+    """Expert GEMM engine for calls without an expert-parallel exchange: ``auto`` (default),
+    ``fused``, ``single`` or ``pair`` (prism_moe_set_expert_engine)."""
+    if name not in ENGINES:
+        raise RuntimeError(f"unknown expert engine {name!r}; one of {sorted(ENGINES)}")
+    check(load().prism_moe_set_expert_engine(ENGINES[name]), "prism_moe_set_expert_engine")
+
+
+def set_wait_limits(wait_ns: int = 0, peer_wait_ns: int = 0) -> None:
+    """Bounds of the kernels' waits on their own pipeline and on other ranks (0 = default)."""
+    check(load().prism_moe_set_wait_limits(int(wait_ns), int(peer_wait_ns)),
+          "prism_moe_set_wait_limits")
+
+
+def ep_read_stats(workspace, device=None) -> dict:
+    """Statistics of the last expert-parallel step that used ``workspace`` (synchronises)."""
+    dev = workspace.device if device is None else device
+    buf = (ctypes.c_uint64 * len(EP_STATS_FIELDS))()
+    check(load().prism_moe_ep_read_stats(ptr(workspace), buf, stream_of(dev)),
+          "prism_moe_ep_read_stats")
+    return dict(zip(EP_STATS_FIELDS, (int(v) for v in buf)))

@@ -1,7 +1,11 @@
 // extern "C" entry points of libprism_moe.so (declared in include/prism_moe.h).
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
+#include <set>
+#include <utility>
 
 #include "common.cuh"
 #include "internal.h"
@@ -28,6 +32,30 @@ void set_error(const char* fmt, ...) {
 int cuda_status(cudaError_t e, const char* what) {
   set_error("%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
   return PRISM_MOE_ERR_CUDA;
+}
+
+namespace {
+std::atomic<int> g_engine{PRISM_MOE_ENGINE_AUTO};
+std::atomic<uint64_t> g_wait_ns{2000000000ull};        // 2 s: far above any legitimate wait
+std::atomic<uint64_t> g_peer_wait_ns{10000000000ull};  // 10 s: peers may start a step late
+std::mutex g_attr_mu;
+std::set<std::pair<const void*, int>> g_attr_done;
+}  // namespace
+
+int expert_engine_setting() { return g_engine.load(std::memory_order_relaxed); }
+uint64_t wait_limit_ns() { return g_wait_ns.load(std::memory_order_relaxed); }
+uint64_t peer_wait_limit_ns() { return g_peer_wait_ns.load(std::memory_order_relaxed); }
+
+int ensure_smem_attr(const void* func, int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(g_attr_mu);
+  if (g_attr_done.count({func, dev})) return PRISM_MOE_OK;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
+  g_attr_done.insert({func, dev});
+  return PRISM_MOE_OK;
 }
 
 int num_sms() {
@@ -235,7 +263,7 @@ int prism_moe_block_forward(const void* x, const void* router_logits, int dtype,
   if (r) return r;
   record_stage(1, st);
   r = build_plan(ids, num_tokens, top_k, num_experts, 1, nullptr, nullptr, nullptr, counts, offsets,
-                 entry_row, nullptr, ws + L.plan, L.plan_bytes, st);
+                 entry_row, nullptr, ws + L.plan, L.plan_bytes, st, err);
   if (r) return r;
   record_stage(2, st);
   r = permute_rows(x, num_tokens, hidden * elem_size(dtype), top_k, entry_row, xs, st);
@@ -261,6 +289,24 @@ int prism_moe_profile_events(void* const* events, int32_t count) {
   for (int i = 0; i < kNumStageEvents; ++i)
     g_stage_events[i] = i < count ? static_cast<cudaEvent_t>(events[i]) : nullptr;
   g_num_stage_events = count;
+  return PRISM_MOE_OK;
+}
+
+int prism_moe_set_expert_engine(int engine) {
+  PRISM_CHECK_ARG(engine >= PRISM_MOE_ENGINE_AUTO && engine <= PRISM_MOE_ENGINE_PAIR,
+                  "set_expert_engine: unknown engine %d", engine);
+  g_engine.store(engine, std::memory_order_relaxed);
+  return PRISM_MOE_OK;
+}
+
+int prism_moe_set_wait_limits(int64_t wait_ns, int64_t peer_wait_ns) {
+  PRISM_CHECK_ARG(wait_ns >= 0 && peer_wait_ns >= 0, "set_wait_limits: negative limit");
+  PRISM_CHECK_ARG(wait_ns <= 60000000000ll && peer_wait_ns <= 60000000000ll,
+                  "set_wait_limits: limits above 60 s are not accepted");
+  g_wait_ns.store(wait_ns > 0 ? static_cast<uint64_t>(wait_ns) : 2000000000ull,
+                  std::memory_order_relaxed);
+  g_peer_wait_ns.store(peer_wait_ns > 0 ? static_cast<uint64_t>(peer_wait_ns) : 10000000000ull,
+                       std::memory_order_relaxed);
   return PRISM_MOE_OK;
 }
 

@@ -7,6 +7,7 @@
 // parameter for the common top-k values (rows and weights stay in registers); other k use a
 // generic loop.
 #include "common.cuh"
+#include "internal.h"
 
 namespace prism {
 namespace {
@@ -53,11 +54,14 @@ template <bool kBf16, int kK>
 __global__ void __launch_bounds__(256)
     combine_kernel(const uint4* __restrict__ y, const int32_t* __restrict__ entry_row,
                    const void* __restrict__ w, int64_t T, int k_rt, int64_t vpr,
-                   uint4* __restrict__ out) {
+                   uint4* __restrict__ out, CombineSource src) {
   constexpr int kEl = kBf16 ? 8 : 4;
   const int lane = threadIdx.x & 31;
   const int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   if (t >= T) return;
+  if (src.gate_err && *reinterpret_cast<const volatile int*>(src.gate_err) == PRISM_MOE_ERR_TIMEOUT)
+    return;   // the step's exchange did not complete: its rows are not all there
+  if (src.parity) y += static_cast<int64_t>(*src.parity & 1u) * (src.parity_stride_bytes / 16);
   const int k = kK > 0 ? kK : k_rt;
   // lane j < k fetches slot j's row and weight once; broadcast by shuffle
   int64_t my_row = -1;
@@ -104,32 +108,35 @@ __global__ void __launch_bounds__(256)
 
 template <bool kBf16>
 void launch_combine(const void* y, const int32_t* entry_row, const void* w, int64_t T, int k,
-                    int64_t vpr, void* out, cudaStream_t st) {
+                    int64_t vpr, void* out, const CombineSource& src, cudaStream_t st) {
   const unsigned blocks = static_cast<unsigned>(ceil_div(T * 32, 256));
   const uint4* yv = static_cast<const uint4*>(y);
   uint4* ov = static_cast<uint4*>(out);
   switch (k) {
-    case 8: combine_kernel<kBf16, 8><<<blocks, 256, 0, st>>>(yv, entry_row, w, T, k, vpr, ov); break;
-    case 4: combine_kernel<kBf16, 4><<<blocks, 256, 0, st>>>(yv, entry_row, w, T, k, vpr, ov); break;
-    case 2: combine_kernel<kBf16, 2><<<blocks, 256, 0, st>>>(yv, entry_row, w, T, k, vpr, ov); break;
-    case 1: combine_kernel<kBf16, 1><<<blocks, 256, 0, st>>>(yv, entry_row, w, T, k, vpr, ov); break;
-    default: combine_kernel<kBf16, 0><<<blocks, 256, 0, st>>>(yv, entry_row, w, T, k, vpr, ov);
+    case 8: combine_kernel<kBf16, 8><<<blocks, 256, 0, st>>>(yv, entry_row, w, T, k, vpr, ov, src); break;
+    case 4: combine_kernel<kBf16, 4><<<blocks, 256, 0, st>>>(yv, entry_row, w, T, k, vpr, ov, src); break;
+    case 2: combine_kernel<kBf16, 2><<<blocks, 256, 0, st>>>(yv, entry_row, w, T, k, vpr, ov, src); break;
+    case 1: combine_kernel<kBf16, 1><<<blocks, 256, 0, st>>>(yv, entry_row, w, T, k, vpr, ov, src); break;
+    default: combine_kernel<kBf16, 0><<<blocks, 256, 0, st>>>(yv, entry_row, w, T, k, vpr, ov, src);
   }
 }
 
 }  // namespace
 
 int combine(const void* y, int dtype, const int32_t* entry_row, const void* w, int64_t T, int k,
-            int64_t hidden, void* out, cudaStream_t st) {
+            int64_t hidden, void* out, cudaStream_t st, const CombineSource* src) {
   const int64_t el = dtype == PRISM_MOE_BF16 ? 2 : 4;
   PRISM_CHECK_ARG((hidden * el) % 16 == 0, "combine: hidden*elem_size must be a multiple of 16");
   PRISM_CHECK_ARG(k >= 1 && k <= 32, "combine: top_k %d outside [1, 32]", k);
+  PRISM_CHECK_ARG(!src || src->parity_stride_bytes % 16 == 0, "combine: parity stride alignment");
   if (T == 0) return PRISM_MOE_OK;
   const int64_t vpr = hidden * el / 16;
+  const CombineSource plain{};
+  const CombineSource& s = src ? *src : plain;
   if (dtype == PRISM_MOE_BF16)
-    launch_combine<true>(y, entry_row, w, T, k, vpr, out, st);
+    launch_combine<true>(y, entry_row, w, T, k, vpr, out, s, st);
   else
-    launch_combine<false>(y, entry_row, w, T, k, vpr, out, st);
+    launch_combine<false>(y, entry_row, w, T, k, vpr, out, s, st);
   PRISM_LAUNCH_CHECK("combine_kernel launch");
   return PRISM_MOE_OK;
 }

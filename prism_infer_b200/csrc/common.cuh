@@ -45,6 +45,17 @@ inline size_t align_up(size_t a, size_t b) { return (a + b - 1) / b * b; }
 
 int num_sms();
 
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) for ``func`` on the current device, done once
+// per (function, device): the attribute belongs to a device context, so a process that drives
+// several GPUs needs it on each.
+int ensure_smem_attr(const void* func, int bytes);
+
+// Process-wide settings (prism_moe_set_expert_engine, prism_moe_set_wait_limits).
+int expert_engine_setting();
+uint64_t wait_limit_ns();        // waits on this GPU's own pipeline
+uint64_t peer_wait_limit_ns();   // waits on other ranks
+constexpr uint64_t kDrainNs = 100000000ull;   // 100 ms: in-flight copies / MMAs after an abort
+
 // Optional profiling hook (prism_moe_profile_events): CUDA events recorded on the launching
 // stream at stage boundaries. Slots: 0 route begin, 1 plan begin, 2 permute begin,
 // 3 gate_up begin, 4 down begin, 5 combine begin, 6 combine end.

@@ -220,7 +220,7 @@ size_t dispatch_workspace_size(int64_t N, int E, int W) {
 int build_plan(const int64_t* ids, int64_t T, int k, int E, int W, int64_t* perm,
                int64_t* splits, int64_t* sorted_leid, int32_t* counts, int32_t* offsets,
                int32_t* entry_row, int32_t* row_entry, void* ws, size_t ws_bytes,
-               cudaStream_t st) {
+               cudaStream_t st, int* err_out) {
   const int64_t N = T * k;
   PRISM_CHECK_ARG(E >= 1 && E <= kMaxKeys, "num_experts %d outside [1, %d]", E, kMaxKeys);
   PRISM_CHECK_ARG(W >= 1 && E % W == 0, "num_experts %d not divisible by ep_size %d", E, W);
@@ -231,7 +231,7 @@ int build_plan(const int64_t* ids, int64_t T, int k, int E, int W, int64_t* perm
   const int El = E / W;
   const int64_t nchunks = ceil_div(N > 0 ? N : 1, kChunk);
   char* p = static_cast<char*>(ws);
-  int* err = reinterpret_cast<int*>(p);
+  int* err = err_out ? err_out : reinterpret_cast<int*>(p);   // where ERR_ARG for ids goes
   p += 256;
   int32_t* rank_e = reinterpret_cast<int32_t*>(p);
   p += align_up(sizeof(int32_t) * N, 256);

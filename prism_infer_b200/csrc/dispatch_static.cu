@@ -14,9 +14,13 @@
 // Set-up: the first call on a device looks up the array's device address with
 // cudaGetSymbolAddress, with that device current, and caches it; make that first call before
 // any stream capture begins. All calls on a device share the one array and it keeps the last
-// call's contents; the error word is cleared at the start of every call and every other byte a
-// call reads is written by that call first. Calls whose kernels overlap on the GPU (different
-// streams, or different host threads) race on the array: serialise them.
+// call's contents; the plan's error word (its first bytes) is cleared at the start of every call
+// and every other byte a call reads is written by that call first. Calls whose kernels overlap on
+// the GPU (different streams, or different host threads) race on the array: serialise them.
+//
+// Expert ids must lie in [0, num_experts). Entries outside it are left out of the outputs, as in
+// prism_moe_build_dispatch_plan; the kernel records that in the array's error word, which this
+// entry point does not read back, so the caller is not told.
 #include <mutex>
 
 #include "common.cuh"

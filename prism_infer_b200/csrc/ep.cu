@@ -23,7 +23,15 @@
 // recv buffers (per-segment arrival counters) while its producer waits only for the segment
 // each gate_up tile reads, and whose down epilogue stores every output row into its source
 // rank's back buffer; its last CTA signals C -> wait C -> local combine.
-// Every wait is bounded (kPeerWaitNs); a wait that runs out records PRISM_MOE_ERR_TIMEOUT.
+// Every wait is bounded (prism_moe_set_wait_limits; 10 s by default); a wait that runs out
+// records PRISM_MOE_ERR_TIMEOUT, and the later kernels of that step then do nothing (their
+// tables may describe rows that never arrive).
+//
+// Epoch. The step's epoch (the flag value; its parity picks the buffers) lives in the workspace
+// (EpStepState): ep_counts_kernel sets it — from the caller's ``epoch`` argument, or, when that is
+// 0, by incrementing the workspace's counter — and every later kernel of the step reads it there.
+// With the device counter no launch argument changes from step to step, so a step can be
+// captured once in a CUDA graph and replayed.
 #include <algorithm>
 #include <cstring>
 
@@ -33,11 +41,11 @@
 namespace prism {
 namespace {
 
-constexpr uint64_t kPeerWaitNs = 10000000000ull;  // 10 s: peers may start a step late
 constexpr int kMaxRanks = 64;
 constexpr int kMaxExperts = 1024;
 // flags (2 x 64 x 8 B, padded to 4 KB) + arrival counters (2 x 1024 x 4 B); zero at allocation
 constexpr size_t kHeaderBytes = 4096 + 2 * kMaxExperts * sizeof(uint32_t);
+constexpr size_t kCountsMaxBytes = sizeof(int32_t) * 2 * kMaxRanks * kMaxExperts;
 
 struct Landing {
   size_t flags, arrive, counts, recv, back, total;
@@ -92,7 +100,7 @@ EpWs ep_ws_layout(int64_t max_tokens, int64_t H, int64_t I, int E, int k, int W,
   L.seg_base = take(sizeof(uint64_t) * E);
   L.dst_base = take(sizeof(int32_t) * E);
   L.flag_c = take(sizeof(uint64_t) * W);
-  L.done = take(sizeof(unsigned int) * 4);
+  L.done = take(sizeof(unsigned int) * 4);   // chunk claim, chunks stored, CTAs done
   L.h = take(expert_scratch_bytes(rcap, I, es));
   L.total = o;
   return L;
@@ -103,13 +111,14 @@ __device__ __forceinline__ uint64_t* flag_addr(uint64_t base, size_t flags_off, 
   return reinterpret_cast<uint64_t*>(base + flags_off) + phase * W + slot;
 }
 
-__device__ bool wait_flags(const uint64_t* local_flags, int W, uint64_t epoch, int* err) {
+__device__ bool wait_flags(const uint64_t* local_flags, int W, uint64_t epoch, int* err,
+                           uint64_t limit_ns) {
   const int s = threadIdx.x;
   bool ok = true;
   if (s < W) {
     const uint64_t t0 = global_timer_ns();
     while (load_acquire_sys(local_flags + s) != epoch) {
-      if (global_timer_ns() - t0 > kPeerWaitNs) {
+      if (global_timer_ns() - t0 > limit_ns) {
         record_device_error(err, PRISM_MOE_ERR_TIMEOUT);
         ok = false;
         break;
@@ -143,19 +152,58 @@ __device__ int32_t block_excl_scan(int32_t v, int n, int32_t* tmp, int32_t* tota
 // expert-major order. Source s writes to destinations in the order s, s+1, ... (mod W), so the
 // rows it sends to d arrive j = (d - s) mod W slots into its sequence, and d's GEMM reads the
 // segments of the sources that are done first.
-__global__ void __launch_bounds__(1024)
-    ep_counts_kernel(const int32_t* __restrict__ my_counts, const uint64_t* __restrict__ peers,
-                     size_t flags_off, size_t counts_off, size_t back_off, int64_t row_bytes,
-                     int W, int me, int E, uint64_t epoch, int32_t* __restrict__ seg_offsets,
-                     int32_t* __restrict__ seg_expert, uint64_t* __restrict__ seg_base,
-                     int32_t* __restrict__ dst_base, uint64_t* __restrict__ flag_c,
-                     uint32_t* __restrict__ next_arrive, unsigned int* __restrict__ claim,
-                     int* __restrict__ err) {
+struct CountsArgs {
+  const int32_t* my_counts;   // [E] this rank's expert histogram
+  const uint64_t* peers;      // [W] landing zones
+  size_t flags_off, counts_off;
+  size_t back_off, back_stride;       // parity-0 returned-rows buffer, bytes per parity
+  size_t arrive_off, arrive_stride;   // parity-0 arrival counters, bytes per parity
+  int64_t row_bytes;
+  int W, me, E;
+  uint64_t host_epoch;        // 0: take the next value of the workspace's counter
+  EpStepState* step;
+  int32_t* seg_offsets;       // [W*El + 1]
+  int32_t* seg_expert;        // [W*El]
+  uint64_t* seg_base;         // [W*El]
+  int32_t* dst_base;          // [E]
+  uint64_t* flag_c;           // [W]
+  unsigned int* claim;        // [0] chunk claim, [1] chunks stored
+  int* err;
+  uint64_t peer_wait_ns;
+};
+
+__global__ void __launch_bounds__(1024) ep_counts_kernel(const CountsArgs a) {
   __shared__ int32_t tmp[1024];
   __shared__ int32_t total;
   __shared__ int32_t R[kMaxRanks * kMaxRanks];   // R[d * W + s]: rows source s sends to d
+  __shared__ uint64_t s_epoch;
+  const int32_t* __restrict__ my_counts = a.my_counts;
+  const uint64_t* __restrict__ peers = a.peers;
+  const size_t flags_off = a.flags_off, counts_off = a.counts_off;
+  const int W = a.W, me = a.me, E = a.E;
   const int El = E / W;
+  int* err = a.err;
+  // 0. this step's epoch, and the step's statistics reset
+  if (threadIdx.x == 0) {
+    EpStepState* st = a.step;
+    const uint64_t e = a.host_epoch ? a.host_epoch : st->counter + 1;
+    st->counter = e;
+    st->epoch = e;
+    st->disp_t0 = 0;
+    st->disp_t1 = 0;
+    st->fused_t0 = ~0ull;
+    st->fused_t1 = 0;
+    s_epoch = e;
+  }
+  __syncthreads();
+  const uint64_t epoch = s_epoch;
   const int par = static_cast<int>(epoch & 1);
+  const size_t back_off = a.back_off + static_cast<size_t>(par) * a.back_stride;
+  const int64_t row_bytes = a.row_bytes;
+  int32_t* __restrict__ seg_offsets = a.seg_offsets;
+  int32_t* __restrict__ seg_expert = a.seg_expert;
+  uint64_t* __restrict__ seg_base = a.seg_base;
+  int32_t* __restrict__ dst_base = a.dst_base;
   // 1. my histogram into row `me` of every rank's counts[par]
   for (int i = threadIdx.x; i < W * E; i += blockDim.x) {
     const int d = i / E, e = i % E;
@@ -167,7 +215,7 @@ __global__ void __launch_bounds__(1024)
   if (threadIdx.x < W) store_release_sys(flag_addr(peers[threadIdx.x], flags_off, W, 0, me), epoch);
   // 2. wait for every source's histogram
   const uint64_t* my_flags = flag_addr(peers[me], flags_off, W, 0, 0);
-  wait_flags(my_flags, W, epoch, err);
+  wait_flags(my_flags, W, epoch, err, a.peer_wait_ns);
   __syncthreads();
   __threadfence();
   const volatile int32_t* C =
@@ -193,6 +241,16 @@ __global__ void __launch_bounds__(1024)
     R[p] = r;
   }
   __syncthreads();
+  if (i == 0) {   // rows that cross NVLink this step, each way
+    uint64_t send = 0, recv = 0;
+    for (int d = 0; d < W; ++d)
+      if (d != me) {
+        send += static_cast<uint64_t>(R[d * W + me]);
+        recv += static_cast<uint64_t>(R[me * W + d]);
+      }
+    a.step->send_rows = send;
+    a.step->recv_rows = recv;
+  }
   // 5. where my rows of expert e start in its owner's receive layout
   const int32_t mine = i < E ? C[me * E + i] : 0;
   const int32_t my_ex = block_excl_scan(mine, E, tmp, nullptr);
@@ -235,15 +293,25 @@ __global__ void __launch_bounds__(1024)
   //    starts at zero, and so do the next step's arrival counters (the other parity: every row
   //    of the previous step was consumed by this rank's previous gate_up, and no peer adds to
   //    the next step's before it has seen this rank's next A flag).
-  if (i == 0) *claim = 0u;
+  uint32_t* next_arrive = reinterpret_cast<uint32_t*>(
+      peers[me] + a.arrive_off + static_cast<size_t>(par ^ 1) * a.arrive_stride);
+  if (i < 2) a.claim[i] = 0u;
   if (i < E) next_arrive[i] = 0u;
   __threadfence_system();
-  if (i < W) flag_c[i] = reinterpret_cast<uint64_t>(flag_addr(peers[i], flags_off, W, 1, me));
+  if (i < W) a.flag_c[i] = reinterpret_cast<uint64_t>(flag_addr(peers[i], flags_off, W, 1, me));
 }
 
+// Wait until every rank's flag of ``phase`` holds this step's epoch. Skipped when the step's
+// exchange already failed (the flags would never come).
 __global__ void ep_wait_kernel(const uint64_t* __restrict__ peers, int me, size_t flags_off,
-                               int W, int phase, uint64_t epoch, int* __restrict__ err) {
-  wait_flags(flag_addr(peers[me], flags_off, W, phase, 0), W, epoch, err);
+                               int W, int phase, const EpStepState* __restrict__ step,
+                               int* __restrict__ err, uint64_t limit_ns) {
+  __shared__ int s_skip;
+  if (threadIdx.x == 0)
+    s_skip = *reinterpret_cast<const volatile int*>(err) == PRISM_MOE_ERR_TIMEOUT;
+  __syncthreads();
+  if (s_skip) return;
+  wait_flags(flag_addr(peers[me], flags_off, W, phase, 0), W, step->epoch, err, limit_ns);
   __syncthreads();
   __threadfence_system();
 }
@@ -271,7 +339,9 @@ __attribute__((visibility("default"))) int prism_moe_ep_alloc_landing(size_t byt
   PRISM_CHECK_ARG(bytes > 0 && ptr && ipc_handle, "ep_alloc_landing: bad arguments");
   void* p = nullptr;
   PRISM_CUDA(cudaMalloc(&p, bytes));
-  cudaError_t e = cudaMemset(p, 0, kHeaderBytes);   // flags at epoch 0, counters at 0
+  // flags at epoch 0, arrival counters at 0, and the all-gathered histograms at 0 (so that a
+  // step whose counts exchange timed out never derives tables from uninitialised memory)
+  cudaError_t e = cudaMemset(p, 0, std::min(bytes, kHeaderBytes + kCountsMaxBytes));
   if (e == cudaSuccess) {
     cudaIpcMemHandle_t h;
     e = cudaIpcGetMemHandle(&h, p);
@@ -337,7 +407,6 @@ __attribute__((visibility("default"))) int prism_moe_ep_forward(
                   static_cast<long long>(num_tokens), static_cast<long long>(max_tokens));
   PRISM_CHECK_ARG(num_tokens == 0 || router_logits || (topk_ids_in && topk_weights_in),
                   "ep_forward: needs router_logits or topk ids and weights");
-  PRISM_CHECK_ARG(epoch > 0, "ep_forward: epoch must be >= 1 and increase every step");
   PRISM_CHECK_ARG(my_landing && peer_landing && w_gate_up && w_down &&
                       (num_tokens == 0 || (x && out)),
                   "ep_forward: null pointer");
@@ -351,8 +420,8 @@ __attribute__((visibility("default"))) int prism_moe_ep_forward(
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(workspace);
   int* err = reinterpret_cast<int*>(ws + L.err);
-  const int par = static_cast<int>(epoch & 1);
-  const int64_t T = num_tokens, N = T * k;
+  EpStepState* step = reinterpret_cast<EpStepState*>(ws + kEpStepOffset);
+  const int64_t T = num_tokens;
   record_stage(0, st);
   const int64_t* ids = topk_ids_in;
   const void* w = topk_weights_in;
@@ -368,8 +437,10 @@ __attribute__((visibility("default"))) int prism_moe_ep_forward(
   int32_t* entry_row = reinterpret_cast<int32_t*>(ws + L.entry_row);
   int32_t* row_entry = reinterpret_cast<int32_t*>(ws + L.row_entry);
   record_stage(1, st);
+  // ids outside [0, E) (caller-given) are left out of the plan and recorded as ERR_ARG in the
+  // step's error word; no row is sent for them and their slots add nothing to the output
   int r = build_plan(ids, T, k, E, 1, nullptr, nullptr, nullptr, counts, offsets, entry_row,
-                     row_entry, ws + L.plan, L.plan_bytes, st);
+                     row_entry, ws + L.plan, L.plan_bytes, st, err);
   if (r) return r;
   record_stage(2, st);   // counts all-gather and the step's tables
   int32_t* seg_offsets = reinterpret_cast<int32_t*>(ws + L.seg_offsets);
@@ -378,16 +449,35 @@ __attribute__((visibility("default"))) int prism_moe_ep_forward(
   int32_t* dst_base = reinterpret_cast<int32_t*>(ws + L.dst_base);
   uint64_t* flag_c = reinterpret_cast<uint64_t*>(ws + L.flag_c);
   unsigned int* done = reinterpret_cast<unsigned int*>(ws + L.done);
-  const size_t recv_off = LL.recv + static_cast<size_t>(par) * LL.rcap * hidden * es;
-  const size_t back_off = LL.back + static_cast<size_t>(par) * LL.bcap * hidden * es;
   char* land = static_cast<char*>(my_landing);
-  const size_t arrive_off = LL.arrive + static_cast<size_t>(par) * E * sizeof(uint32_t);
-  uint32_t* next_arrive =
-      reinterpret_cast<uint32_t*>(land + LL.arrive + static_cast<size_t>(par ^ 1) * E * sizeof(uint32_t));
+  const size_t recv_stride = static_cast<size_t>(LL.rcap) * hidden * es;
+  const size_t back_stride = static_cast<size_t>(LL.bcap) * hidden * es;
+  const size_t arrive_stride = static_cast<size_t>(E) * sizeof(uint32_t);
 
-  ep_counts_kernel<<<1, 1024, 0, st>>>(counts, peer_landing, LL.flags, LL.counts, back_off,
-                                       hidden * es, W, me, E, epoch, seg_offsets, seg_expert,
-                                       seg_base, dst_base, flag_c, next_arrive, done, err);
+  CountsArgs ca{};
+  ca.my_counts = counts;
+  ca.peers = peer_landing;
+  ca.flags_off = LL.flags;
+  ca.counts_off = LL.counts;
+  ca.back_off = LL.back;
+  ca.back_stride = back_stride;
+  ca.arrive_off = LL.arrive;
+  ca.arrive_stride = arrive_stride;
+  ca.row_bytes = hidden * es;
+  ca.W = W;
+  ca.me = me;
+  ca.E = E;
+  ca.host_epoch = epoch;
+  ca.step = step;
+  ca.seg_offsets = seg_offsets;
+  ca.seg_expert = seg_expert;
+  ca.seg_base = seg_base;
+  ca.dst_base = dst_base;
+  ca.flag_c = flag_c;
+  ca.claim = done;
+  ca.err = err;
+  ca.peer_wait_ns = peer_wait_limit_ns();
+  ep_counts_kernel<<<1, 1024, 0, st>>>(ca);
   PRISM_LAUNCH_CHECK("ep_counts_kernel launch");
   // One launch per GPU for the rest of the exchange and the experts: its copy warps dispatch
   // this rank's rows into the owners' receive buffers while its producer waits only for the
@@ -396,17 +486,22 @@ __attribute__((visibility("default"))) int prism_moe_ep_forward(
   GemmDispatch disp{};
   disp.x = x;
   disp.vpr = hidden * es / 16;
-  disp.n_rows = N;
   disp.k = k;
+  disp.E = E;
   disp.ids = ids;
   disp.row_entry = row_entry;
   disp.expert_offsets = offsets;
   disp.dst_base = dst_base;
   disp.peers = peer_landing;
-  disp.recv_off = recv_off;
-  disp.arrive_off = arrive_off;
-  disp.my_arrive = reinterpret_cast<const uint32_t*>(land + arrive_off);
+  for (int p = 0; p < 2; ++p) {
+    disp.recv_off[p] = LL.recv + p * recv_stride;
+    disp.arrive_off[p] = LL.arrive + p * arrive_stride;
+    disp.x_recv[p] = land + disp.recv_off[p];
+  }
+  disp.epoch_ptr = &step->epoch;
   disp.claim = done;
+  disp.step = step;
+  disp.gate_err = err;
   disp.W = W;
   disp.me = me;
   disp.El = El;
@@ -414,16 +509,33 @@ __attribute__((visibility("default"))) int prism_moe_ep_forward(
   down.seg_base = seg_base;
   down.signal_flags = reinterpret_cast<uint64_t* const*>(flag_c);
   down.num_signal = W;
-  down.epoch = epoch;
-  down.done_counter = done + 1;
-  r = expert_swiglu_bf16(land + recv_off, LL.rcap, hidden, inter, seg_offsets, seg_expert, E, El,
+  down.epoch_ptr = &step->epoch;
+  down.done_counter = done + 2;
+  down.step = step;
+  r = expert_swiglu_bf16(land + LL.recv, LL.rcap, hidden, inter, seg_offsets, seg_expert, E, El,
                          w_gate_up, w_down, nullptr, ws + L.h, err, st, &down, &disp);
   if (r) return r;
-  ep_wait_kernel<<<1, 64, 0, st>>>(peer_landing, me, LL.flags, W, 1, epoch, err);
+  ep_wait_kernel<<<1, 64, 0, st>>>(peer_landing, me, LL.flags, W, 1, step, err,
+                                   peer_wait_limit_ns());
   PRISM_LAUNCH_CHECK("ep_wait_kernel launch");
-  r = combine(land + back_off, dtype, entry_row, w, T, k, hidden, out, st);
+  CombineSource src{};
+  src.parity = &step->epoch;
+  src.parity_stride_bytes = static_cast<int64_t>(back_stride);
+  src.gate_err = err;
+  r = combine(land + LL.back, dtype, entry_row, w, T, k, hidden, out, st, &src);
   record_stage(6, st);
   return r;
+}
+
+__attribute__((visibility("default"))) int prism_moe_ep_read_stats(const void* workspace,
+                                                                   uint64_t* stats,
+                                                                   void* stream) {
+  PRISM_CHECK_ARG(workspace && stats, "ep_read_stats: null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  PRISM_CUDA(cudaMemcpyAsync(stats, static_cast<const char*>(workspace) + kEpStepOffset,
+                             sizeof(EpStepState), cudaMemcpyDeviceToHost, st));
+  PRISM_CUDA(cudaStreamSynchronize(st));
+  return PRISM_MOE_OK;
 }
 
 }  // extern "C"

@@ -29,8 +29,6 @@
 // launches are faster (every CTA works on one weight stream at a time), with an exchange the
 // fused launch is.
 #include <algorithm>
-#include <cstdlib>
-#include <mutex>
 
 #include "gemm_sm100.cuh"
 
@@ -67,6 +65,8 @@ struct FusedParams {
   int kb_dn = 0;   // down k-blocks: ceil(I / 64)
   int lag = 1;     // L, in m-tiles
   int64_t H = 0, I = 0;
+  uint64_t wait_ns = 0;        // bound of every wait on this GPU's own pipeline
+  uint64_t peer_wait_ns = 0;   // bound of a wait for rows from other ranks
   uint16_t* h = nullptr;               // [rows_cap, I]
   uint16_t* y = nullptr;               // [rows_cap, H] unless the output has seg_base
   unsigned int* claim = nullptr;       // tile claim counter, zero at launch
@@ -111,15 +111,15 @@ __device__ __forceinline__ void add_release_gpu(unsigned int* p, uint32_t v) {
 // ---------------------------------------------------------------------------------------------
 // Dispatch: ``n`` rows of expert ``e`` are written; publish them to the owner's arrival counter
 // of the receive segment they belong to.
-__device__ __forceinline__ void dispatch_flush(const GemmDispatch& D, int64_t e, unsigned int n,
-                                               int lane) {
+__device__ __forceinline__ void dispatch_flush(const GemmDispatch& D, size_t arrive_off,
+                                               int64_t e, unsigned int n, int lane) {
   __threadfence_system();
   __syncwarp();
   if (lane == 0) {
     const int d = static_cast<int>(e / D.El);
     const int j = (d - D.me + D.W) % D.W;
     const int sg = j * D.El + static_cast<int>(e - static_cast<int64_t>(d) * D.El);
-    add_release_sys(reinterpret_cast<uint32_t*>(D.peers[d] + D.arrive_off) + sg, n);
+    add_release_sys(reinterpret_cast<uint32_t*>(D.peers[d] + arrive_off) + sg, n);
   }
   __syncwarp();
 }
@@ -145,25 +145,27 @@ __device__ __forceinline__ void copy_row_pair(const uint4* sa, uint4* da, const 
   }
 }
 
-// One 16-row dispatch chunk of this rank's expert-major rows, own block first and then the
-// following ranks' blocks. Lanes look up the chunk's rows at once; rows then move in pairs.
-__device__ void dispatch_chunk(const GemmDispatch& D, int64_t c, int lane) {
+// One 16-row dispatch chunk of this rank's expert-major rows [0, n), own block first and then
+// the following ranks' blocks. Lanes look up the chunk's rows at once; rows then move in pairs.
+// Every row below n belongs to an entry with a valid expert id (the plan leaves the others out),
+// so every store lands inside an owner's receive buffer.
+__device__ void dispatch_chunk(const GemmDispatch& D, int64_t c, int64_t n, int par, int lane) {
   constexpr int kChunkRows = 16;
-  const int64_t N = D.n_rows;
   const int64_t shift = D.expert_offsets[D.me * D.El];
   const int64_t i0 = c * kChunkRows;
-  const int nr = static_cast<int>(N - i0 < kChunkRows ? N - i0 : kChunkRows);
+  const int nr = static_cast<int>(n - i0 < kChunkRows ? n - i0 : kChunkRows);
   const uint4* x = static_cast<const uint4*>(D.x);
+  const size_t recv_off = D.recv_off[par], arrive_off = D.arrive_off[par];
   int64_t my_e = -1, my_src = 0;
   uint64_t my_dst = 0;
   if (lane < nr) {
-    const int64_t q = (i0 + lane + shift) % N;
+    const int64_t q = (i0 + lane + shift) % n;
     const int32_t f = D.row_entry[q];
     my_e = D.ids[f];
     my_src = f / D.k;
     const int d = static_cast<int>(my_e / D.El);
     const int64_t dst_row = D.dst_base[my_e] + (q - D.expert_offsets[my_e]);
-    my_dst = D.peers[d] + D.recv_off + static_cast<uint64_t>(dst_row * D.vpr * 16);
+    my_dst = D.peers[d] + recv_off + static_cast<uint64_t>(dst_row * D.vpr * 16);
   }
   int64_t e_run = -1;
   unsigned int n_run = 0;
@@ -179,26 +181,35 @@ __device__ void dispatch_chunk(const GemmDispatch& D, int64_t c, int lane) {
     for (int t = r; t <= rb; ++t) {
       const int64_t e = __shfl_sync(0xffffffffu, my_e, t);
       if (e != e_run) {
-        if (n_run) dispatch_flush(D, e_run, n_run, lane);
+        if (n_run) dispatch_flush(D, arrive_off, e_run, n_run, lane);
         e_run = e;
         n_run = 0;
       }
       ++n_run;
     }
   }
-  if (n_run) dispatch_flush(D, e_run, n_run, lane);
+  if (n_run) dispatch_flush(D, arrive_off, e_run, n_run, lane);
 }
 
-// Copy-warp loop: claim 16-row dispatch chunks until none are left.
-__device__ void copy_warp_loop(const GemmDispatch& D, int lane) {
+// Copy-warp loop: claim 16-row dispatch chunks until none are left. The rows to send are the
+// plan's valid rows, expert_offsets[E] of them. The warp that claims the first chunk and the
+// warp that stores the last one stamp the step's dispatch window.
+__device__ void copy_warp_loop(const GemmDispatch& D, int par, int lane) {
   constexpr int kChunkRows = 16;
-  const int64_t nchunks = (D.n_rows + kChunkRows - 1) / kChunkRows;
+  const int64_t n = D.expert_offsets[D.E];
+  const int64_t nchunks = (n + kChunkRows - 1) / kChunkRows;
   for (;;) {
     unsigned int claimed = 0;
     if (lane == 0) claimed = atomicAdd(D.claim, 1u);
     const int64_t c = __shfl_sync(0xffffffffu, claimed, 0);
     if (c >= nchunks) break;
-    dispatch_chunk(D, c, lane);
+    if (c == 0 && lane == 0 && D.step) D.step->disp_t0 = global_timer_ns();
+    dispatch_chunk(D, c, n, par, lane);
+    if (lane == 0) {
+      const unsigned int stored = atomicAdd(D.claim + 1, 1u);
+      if (stored + 1 == static_cast<unsigned int>(nchunks) && D.step)
+        D.step->disp_t1 = global_timer_ns();
+    }
   }
 }
 
@@ -208,12 +219,28 @@ __device__ void copy_warp_loop(const GemmDispatch& D, int lane) {
 template <bool kDispatch>
 __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
     fused_experts_kernel(const __grid_constant__ CUtensorMap map_x,
+                         const __grid_constant__ CUtensorMap map_x1,
                          const __grid_constant__ CUtensorMap map_wgu,
                          const __grid_constant__ CUtensorMap map_h,
                          const __grid_constant__ CUtensorMap map_wd, FusedParams P,
                          GemmOutput tgt, GemmDispatch disp) {
   using F = FusedCfg;
   extern __shared__ uint8_t smem_raw[];
+  // An expert-parallel step whose exchange already failed (a peer wait ran out) runs nothing:
+  // its tables may describe rows that never arrive.
+  __shared__ int s_skip;
+  if (threadIdx.x == 0) {
+    s_skip = kDispatch && disp.gate_err &&
+             *reinterpret_cast<const volatile int*>(disp.gate_err) == PRISM_MOE_ERR_TIMEOUT;
+    if (!s_skip && tgt.step)
+      atomicMin(reinterpret_cast<unsigned long long*>(&tgt.step->fused_t0),
+                static_cast<unsigned long long>(global_timer_ns()));
+  }
+  __syncthreads();
+  if (s_skip) return;
+  // receive-buffer parity of this step (expert parallelism; always 0 otherwise)
+  const int par = kDispatch ? static_cast<int>(*disp.epoch_ptr & 1u) : 0;
+  const CUtensorMap* map_a = par ? &map_x1 : &map_x;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* stages = smem;
@@ -247,7 +274,7 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
     mbar_init(drain, 1);
     *abort = 0;
     fence_mbar_init();
-    tma_prefetch_desc(&map_x);
+    tma_prefetch_desc(map_a);
     tma_prefetch_desc(&map_wgu);
     tma_prefetch_desc(&map_h);
     tma_prefetch_desc(&map_wd);
@@ -275,13 +302,16 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
     int ready_seg = -1;      // dispatch: every row of this segment has landed
     int32_t ready_mt = -1;   // every h row of this m-tile is stored
     bool ok = true;
+    const uint32_t* my_arrive =
+        kDispatch ? reinterpret_cast<const uint32_t*>(disp.peers[disp.me] + disp.arrive_off[par])
+                  : nullptr;
     for (;;) {
       int32_t t = -1;
       {
         const unsigned int c = atomicAdd(P.claim, 1u);
         if (c < static_cast<unsigned int>(total)) t = static_cast<int32_t>(c);
       }
-      if (!mbar_wait_bounded(&ring_empty[rslot], rphase ^ 1, abort, kWaitNs)) {
+      if (!mbar_wait_bounded(&ring_empty[rslot], rphase ^ 1, abort, P.wait_ns)) {
         ok = false;
         break;
       }
@@ -300,8 +330,8 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
       if (tr.kind == 0) {
         if (kDispatch && s != ready_seg) {
           const uint32_t need = static_cast<uint32_t>(P.seg_offsets[s + 1] - P.seg_offsets[s]);
-          while (load_acquire_sys(disp.my_arrive + s) != need) {
-            if (*abort || global_timer_ns() - t0 > kPeerWaitNs) {
+          while (load_acquire_sys(my_arrive + s) != need) {
+            if (*abort || global_timer_ns() - t0 > P.peer_wait_ns) {
               ok = false;
               break;
             }
@@ -312,7 +342,7 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
         }
       } else if (tr.mt != ready_mt) {
         while (load_acquire_gpu(P.h_ready + tr.mt) != h_target) {
-          if (*abort || global_timer_ns() - t0 > kWaitNs) {
+          if (*abort || global_timer_ns() - t0 > P.wait_ns) {
             ok = false;
             break;
           }
@@ -323,7 +353,7 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
       if (!ok) break;
       const int nkb = tr.kind == 0 ? P.kb_gu : P.kb_dn;
       for (int kb = 0; kb < nkb; ++kb) {
-        if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort, kWaitNs)) {
+        if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort, P.wait_ns)) {
           ok = false;
           break;
         }
@@ -331,7 +361,7 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
         uint8_t* sb = sa + F::kABytes;
         mbar_arrive_expect_tx(&full[stage], F::kTxBytes);
         if (tr.kind == 0) {
-          tma_load_2d(sa, &map_x, &full[stage], kb * kBK, row0);
+          tma_load_2d(sa, map_a, &full[stage], kb * kBK, row0);
           // gate rows then up rows of n-tile nt in one copy (box spans both halves)
           tma_load_4d(sb, &map_wgu, &full[stage], kb * kBK, tr.nt * 128, 0, e);
         } else {
@@ -364,7 +394,7 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
     uint32_t rphase = 0;
     bool ok = true;
     for (int it = 0;; ++it) {
-      if (!mbar_wait_bounded(&ring_full[rslot], rphase, abort, kWaitNs)) {
+      if (!mbar_wait_bounded(&ring_full[rslot], rphase, abort, P.wait_ns)) {
         ok = false;
         break;
       }
@@ -378,14 +408,14 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
       const int nkb = tile_at(t, M, P.n_gu, P.n_dn, P.lag).kind == 0 ? P.kb_gu : P.kb_dn;
       const int buf = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
-      if (!mbar_wait_bounded(&acc_empty[buf], acc_phase ^ 1, abort, kWaitNs)) {
+      if (!mbar_wait_bounded(&acc_empty[buf], acc_phase ^ 1, abort, P.wait_ns)) {
         ok = false;
         break;
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + buf * kBN;
       for (int kb = 0; kb < nkb; ++kb) {
-        if (!mbar_wait_bounded(&full[stage], phase, abort, kWaitNs)) {
+        if (!mbar_wait_bounded(&full[stage], phase, abort, P.wait_ns)) {
           ok = false;
           break;
         }
@@ -416,7 +446,7 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
     }
   } else if (kDispatch && warp >= 6) {
     // ------------------------------------------------------------------ copy warps
-    copy_warp_loop(disp, lane);
+    copy_warp_loop(disp, par, lane);
   } else if (warp >= 2) {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
@@ -425,7 +455,7 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
     int rslot = 0;
     uint32_t rphase = 0;
     for (int it = 0;; ++it) {
-      if (!mbar_wait_bounded(&ring_full[rslot], rphase, abort, kWaitNs)) {
+      if (!mbar_wait_bounded(&ring_full[rslot], rphase, abort, P.wait_ns)) {
         *abort = 1;
         record_device_error(P.err, PRISM_MOE_ERR_TIMEOUT);
         break;
@@ -445,7 +475,7 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
       const int32_t row0 = P.seg_offsets[s] + (tr.mt - prefix[s]) * 128;
       const int32_t seg_end = P.seg_offsets[s + 1];
       const int32_t rows_valid = (seg_end < P.rows_cap ? seg_end : P.rows_cap) - row0;
-      if (!mbar_wait_bounded(&acc_full[buf], acc_phase, abort, kWaitNs)) {
+      if (!mbar_wait_bounded(&acc_full[buf], acc_phase, abort, P.wait_ns)) {
         *abort = 1;
         record_device_error(P.err, PRISM_MOE_ERR_TIMEOUT);
         break;
@@ -491,25 +521,23 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
     const unsigned int prev = atomicAdd(tgt.done_counter, 1u);
     if (prev == gridDim.x - 1) {
       *tgt.done_counter = 0u;  // ready for the next launch (stream-ordered)
+      if (tgt.step) tgt.step->fused_t1 = global_timer_ns();
       __threadfence_system();
-      for (int i = 0; i < tgt.num_signal; ++i) store_release_sys(tgt.signal_flags[i], tgt.epoch);
+      const uint64_t ep = tgt.epoch_ptr ? *tgt.epoch_ptr : tgt.epoch;
+      for (int i = 0; i < tgt.num_signal; ++i) store_release_sys(tgt.signal_flags[i], ep);
     }
   }
 }
 
 template <bool kDispatch>
-int launch_fused(const CUtensorMap (&maps)[4], const FusedParams& P, const GemmOutput& tgt,
+int launch_fused(const CUtensorMap (&maps)[5], const FusedParams& P, const GemmOutput& tgt,
                  const GemmDispatch& disp, int grid, cudaStream_t st) {
   auto kern = fused_experts_kernel<kDispatch>;
-  static std::once_flag once;
-  static cudaError_t attr_status = cudaSuccess;
-  std::call_once(once, [&] {
-    attr_status = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(FusedCfg::kSmemBytes));
-  });
-  PRISM_CUDA(attr_status);
+  if (int r = ensure_smem_attr(reinterpret_cast<const void*>(kern),
+                               static_cast<int>(FusedCfg::kSmemBytes)))
+    return r;
   kern<<<grid, kDispatch ? kDispatchThreads : kThreads, FusedCfg::kSmemBytes, st>>>(
-      maps[0], maps[1], maps[2], maps[3], P, tgt, disp);
+      maps[0], maps[4], maps[1], maps[2], maps[3], P, tgt, disp);
   PRISM_LAUNCH_CHECK("fused_experts_kernel launch");
   return PRISM_MOE_OK;
 }
@@ -528,13 +556,22 @@ int expert_swiglu_fused(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
                         const void* wgu, const void* wd, void* y, void* h, unsigned int* sync,
                         int* err, cudaStream_t st, const GemmOutput* down_out,
                         const GemmDispatch* dispatch) {
-  CUtensorMap maps[4];
+  // maps: [0] A rows (parity-0 receive buffer under expert parallelism), [1] gate/up weights,
+  // [2] h, [3] down weights, [4] A rows of the parity-1 receive buffer (= [0] otherwise)
+  CUtensorMap maps[5];
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(H), static_cast<uint64_t>(rows_cap)};
     const uint64_t strides[1] = {static_cast<uint64_t>(H) * 2};
     const uint32_t box[2] = {kBK, 128};
-    int r = encode_bf16_map(&maps[0], xs, 2, dims, strides, box);
+    const bool two = dispatch && dispatch->x_recv[0] && dispatch->x_recv[1];
+    int r = encode_bf16_map(&maps[0], two ? dispatch->x_recv[0] : xs, 2, dims, strides, box);
     if (r) return r;
+    if (two) {
+      r = encode_bf16_map(&maps[4], dispatch->x_recv[1], 2, dims, strides, box);
+      if (r) return r;
+    } else {
+      maps[4] = maps[0];
+    }
   }
   {
     const uint64_t dims[4] = {static_cast<uint64_t>(H), static_cast<uint64_t>(I), 2,
@@ -573,7 +610,8 @@ int expert_swiglu_fused(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
   // A CTA holds up to about three tiles between claiming one and storing its output; a lag of
   // twice that keeps down tiles from waiting for h even when epilogues run slow.
   P.lag = static_cast<int>(std::max<int64_t>(1, ceil_div(6 * grid, P.n_gu + P.n_dn)));
-  if (const char* lg = std::getenv("PRISM_MOE_FUSED_LAG")) P.lag = std::max(1, std::atoi(lg));
+  P.wait_ns = wait_limit_ns();
+  P.peer_wait_ns = peer_wait_limit_ns();
   P.H = H;
   P.I = I;
   P.h = static_cast<uint16_t*>(h);

@@ -29,7 +29,6 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
-#include <cstdlib>
 #include <mutex>
 
 #include "gemm_sm100.cuh"
@@ -45,7 +44,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                               const int32_t* __restrict__ seg_expert, int nseg, int num_kb,
                               int num_n_tiles, int64_t n_out, uint16_t* __restrict__ out,
                               int64_t out_ld, int32_t rows_cap, int* __restrict__ err,
-                              GemmOutput tgt) {
+                              GemmOutput tgt, uint64_t kWaitNs) {
   using C = Cfg<kPair>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -283,7 +282,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (prev == gridDim.x - 1) {
       *tgt.done_counter = 0u;  // ready for the next launch (stream-ordered)
       __threadfence_system();
-      for (int i = 0; i < tgt.num_signal; ++i) store_release_sys(tgt.signal_flags[i], tgt.epoch);
+      const uint64_t ep = tgt.epoch_ptr ? *tgt.epoch_ptr : tgt.epoch;
+      for (int i = 0; i < tgt.num_signal; ++i) store_release_sys(tgt.signal_flags[i], ep);
     }
   }
 }
@@ -341,14 +341,21 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const int32_t* seg
   using C = Cfg<kPair>;
   auto kern = grouped_gemm_sm100_kernel<kMode, kPair>;
   constexpr int threads = kThreads;
-  static std::once_flag once;
-  static cudaError_t attr_status = cudaSuccess;
-  static int max_units = 0;
-  std::call_once(once, [&] {
-    attr_status = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(C::kSmemBytes));
+  if (int r = ensure_smem_attr(reinterpret_cast<const void*>(kern), static_cast<int>(C::kSmemBytes)))
+    return r;
+  // resident scheduling units (CTAs, or CTA pairs) per device, looked up once per device
+  static std::mutex units_mu;
+  static int units_of_dev[64] = {};
+  int dev = 0;
+  PRISM_CUDA(cudaGetDevice(&dev));
+  int max_units = 0;
+  {
+    std::lock_guard<std::mutex> lock(units_mu);
+    max_units = dev >= 0 && dev < 64 ? units_of_dev[dev] : 0;
+  }
+  if (max_units == 0) {
     max_units = num_sms();
-    if (attr_status == cudaSuccess && kPair) {
+    if (kPair) {
       // how many CTA pairs can be resident at once
       cudaLaunchConfig_t cfg = {};
       cudaLaunchAttribute attr[1];
@@ -368,8 +375,9 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const int32_t* seg
         max_units = num_sms() / 2;
       cudaGetLastError();
     }
-  });
-  PRISM_CUDA(attr_status);
+    std::lock_guard<std::mutex> lock(units_mu);
+    if (dev >= 0 && dev < 64) units_of_dev[dev] = max_units;
+  }
   const int n_tile = kMode == kGateUp ? 128 : kBN;
   const int num_n_tiles = static_cast<int>(ceil_div(n_out, n_tile));
   const int num_kb = static_cast<int>(ceil_div(K, kBK));
@@ -392,7 +400,7 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const int32_t* seg
   }
   PRISM_CUDA(cudaLaunchKernelEx(&cfg, kern, ma, mb, seg_offsets, seg_expert, nseg, num_kb,
                                 num_n_tiles, n_out, out, n_out, static_cast<int32_t>(rows_cap),
-                                err, tgt));
+                                err, tgt, wait_limit_ns()));
   return PRISM_MOE_OK;
 }
 
@@ -403,13 +411,13 @@ enum class Engine { kFused, kSingle, kPair };
 // (expert_fused_sm100.cu), so that the dispatch and the down GEMM's stores into peers overlap
 // tensor-core work; so does a step whose segments average under one m-tile (decode: the
 // launch boundary between the GEMMs would idle the GPU while each weight stream runs once,
-// measured 7% slower at 64 tokens). PRISM_MOE_GEMM_ENGINE=fused|single|pair overrides the
-// choice for steps without a dispatch (single = two launches with 128-row tiles).
+// measured 7% slower at 64 tokens). prism_moe_set_expert_engine overrides the choice for steps
+// without a dispatch (single = two launches with 128-row tiles).
 Engine pick_engine(int64_t rows_cap, int nseg, bool dispatch) {
-  const char* force = std::getenv("PRISM_MOE_GEMM_ENGINE");
-  if (dispatch || (force && force[0] == 'f')) return Engine::kFused;
-  if (force && force[0] == 's') return Engine::kSingle;
-  if (force && force[0] == 'p') return Engine::kPair;
+  const int force = expert_engine_setting();
+  if (dispatch || force == PRISM_MOE_ENGINE_FUSED) return Engine::kFused;
+  if (force == PRISM_MOE_ENGINE_SINGLE) return Engine::kSingle;
+  if (force == PRISM_MOE_ENGINE_PAIR) return Engine::kPair;
   const int64_t per_seg = rows_cap / std::max(nseg, 1);
   if (per_seg < 128) return Engine::kFused;
   return per_seg >= 2048 ? Engine::kPair : Engine::kSingle;

@@ -19,10 +19,7 @@ constexpr int kBK = 64;   // 64 bf16 = 128 bytes = one swizzle row
 constexpr int kBN = 256;  // MMA N
 constexpr int kThreads = 192;          // producer, MMA, 4 epilogue warps
 constexpr int kDispatchThreads = 320;  // + 4 copy warps when the EP dispatch runs in the launch
-constexpr uint64_t kPeerWaitNs = 10000000000ull;   // 10 s: peer ranks may start a step late
 constexpr uint32_t kTmemCols = 512;
-constexpr uint64_t kWaitNs = 2000000000ull;    // 2 s: far above any legitimate wait
-constexpr uint64_t kDrainNs = 100000000ull;    // 100 ms
 constexpr int kStageRowBytes = 64 * 2 + 16;   // epilogue staging: 64 bf16 + 16 B pad per row
 constexpr size_t kPrefixBytes = ((kMaxSegments + 1) * 4 + 15) / 16 * 16;
 

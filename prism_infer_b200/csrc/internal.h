@@ -8,17 +8,34 @@
 
 namespace prism {
 
+// State of one expert-parallel step, kept at a fixed offset (kEpStepOffset) of the EP workspace.
+// ep_counts_kernel fills it at the start of every step; the other kernels of the step read the
+// epoch from here, so no kernel takes the epoch as a launch argument and a step can be replayed
+// from a CUDA graph. The timing and row counts are statistics for the caller
+// (prism_moe_ep_read_stats).
+struct EpStepState {
+  uint64_t epoch;               // this step's epoch (flag value; parity = epoch & 1)
+  uint64_t counter;             // last epoch issued on this rank
+  uint64_t disp_t0, disp_t1;    // %globaltimer ns: first dispatch chunk claimed, last one stored
+  uint64_t fused_t0, fused_t1;  // %globaltimer ns: fused expert launch, first CTA in, last out
+  uint64_t send_rows;           // rows this rank sends to other ranks (dispatch, remote only)
+  uint64_t recv_rows;           // rows other ranks send here (returned to them by the down GEMM)
+};
+constexpr size_t kEpStepOffset = 64;   // inside the workspace's first 256-byte block
+
 // Where a grouped GEMM writes its output rows and how it announces completion. Default: dense
 // rows ``out + r * ld``. With ``seg_base``, row r of segment s goes to the address
 // seg_base[s] + (r - seg_offsets[s]) * ld * 2 (any GPU's memory reachable by peer access).
-// With ``done_counter``, the last CTA to finish fences at system scope and stores ``epoch`` to
-// each of the ``num_signal`` flag addresses.
+// With ``done_counter``, the last CTA to finish fences at system scope and stores the epoch
+// (``*epoch_ptr``, or ``epoch`` when that is NULL) to each of the ``num_signal`` flag addresses.
 struct GemmOutput {
   const uint64_t* seg_base = nullptr;
   uint64_t* const* signal_flags = nullptr;
   int num_signal = 0;
   uint64_t epoch = 0;
+  const uint64_t* epoch_ptr = nullptr;
   unsigned int* done_counter = nullptr;
+  EpStepState* step = nullptr;   // launch timing (fused_t0 / fused_t1), or NULL
 };
 
 // Expert-parallel exchange carried out INSIDE the fused expert launch (ep.cu): extra copy warps
@@ -27,21 +44,26 @@ struct GemmOutput {
 // to that receive segment's arrival counter on the owner. The receive layout on rank d is
 // segment (j, le), index j * El + le = rows of local expert le from source (d - j) mod W. The
 // GEMM's producer waits (bounded) until the arrival counter of the segment a tile reads equals
-// the segment's row count.
+// the segment's row count. Every per-parity field is indexed by ``*epoch_ptr & 1``.
+// Only rows [0, expert_offsets[E]) are sent: entries with an expert id outside [0, E) have no
+// row (the dispatch plan leaves them out) and are never copied anywhere.
 struct GemmDispatch {
   const void* x = nullptr;              // [T, H] this rank's token rows
   int64_t vpr = 0;                      // 16-byte vectors per row
-  int64_t n_rows = 0;                   // T * k routed rows
   int k = 1;
+  int E = 1;                            // experts in total (W * El)
   const int64_t* ids = nullptr;         // [T*k] expert of each flat entry
   const int32_t* row_entry = nullptr;   // [T*k] expert-major row -> flat entry
   const int32_t* expert_offsets = nullptr;   // [E+1]
   const int32_t* dst_base = nullptr;    // [E] first row of my expert-e rows in the owner's layout
   const uint64_t* peers = nullptr;      // [W] landing-zone base addresses
-  size_t recv_off = 0;                  // byte offset of this step's receive buffer
-  size_t arrive_off = 0;                // byte offset of this step's [W*El] u32 arrival counters
-  const uint32_t* my_arrive = nullptr;  // the same counters in this rank's landing zone
-  unsigned int* claim = nullptr;        // next 16-row chunk to copy; zero at launch
+  const void* x_recv[2] = {nullptr, nullptr};   // this rank's receive buffers (GEMM A operand)
+  size_t recv_off[2] = {0, 0};          // byte offsets of the receive buffers in a landing zone
+  size_t arrive_off[2] = {0, 0};        // byte offsets of the [W*El] u32 arrival counters
+  const uint64_t* epoch_ptr = nullptr;  // the step's epoch (EpStepState::epoch)
+  unsigned int* claim = nullptr;        // [0] next 16-row chunk to copy, [1] chunks stored
+  EpStepState* step = nullptr;          // dispatch timing, or NULL
+  const int* gate_err = nullptr;        // the launch does nothing when this holds ERR_TIMEOUT
   int W = 1, me = 0, El = 1;
 };
 
@@ -49,11 +71,14 @@ struct GemmDispatch {
 int route_topk(const void* logits, int dtype, int64_t T, int E, int k, int renorm, int64_t* ids,
                void* w, int32_t* counts, cudaStream_t st);
 
-// dispatch.cu — row_entry (row -> flat entry) is an internal output, NULL when not wanted
+// dispatch.cu — row_entry (row -> flat entry) is an internal output, NULL when not wanted.
+// Entries whose expert id lies outside [0, E) are left out of every output (entry_row = -1)
+// and record PRISM_MOE_ERR_ARG in ``err_out`` (NULL: the workspace's first word).
 size_t dispatch_workspace_size(int64_t N, int E, int W);
 int build_plan(const int64_t* ids, int64_t T, int k, int E, int W, int64_t* perm, int64_t* splits,
                int64_t* sorted_leid, int32_t* counts, int32_t* offsets, int32_t* entry_row,
-               int32_t* row_entry, void* ws, size_t ws_bytes, cudaStream_t st);
+               int32_t* row_entry, void* ws, size_t ws_bytes, cudaStream_t st,
+               int* err_out = nullptr);
 int permute_rows(const void* x, int64_t T, int64_t row_bytes, int k, const int32_t* entry_row,
                  void* xs, cudaStream_t st);
 
@@ -92,7 +117,14 @@ int expert_swiglu_f32(const float* x, int64_t rows_cap, int64_t H, int64_t I,
                       const float* wgu, const float* wd, float* y, float* h, cudaStream_t st);
 
 // combine.cu
+// With ``parity`` (EP steps): the rows are read from y + (*parity & 1) * parity_stride_bytes,
+// and a launch whose ``gate_err`` word holds PRISM_MOE_ERR_TIMEOUT writes nothing.
+struct CombineSource {
+  const uint64_t* parity = nullptr;
+  int64_t parity_stride_bytes = 0;
+  const int* gate_err = nullptr;
+};
 int combine(const void* y, int dtype, const int32_t* entry_row, const void* w, int64_t T, int k,
-            int64_t hidden, void* out, cudaStream_t st);
+            int64_t hidden, void* out, cudaStream_t st, const CombineSource* src = nullptr);
 
 }  // namespace prism

@@ -92,8 +92,9 @@ class ExpertParallelMoE(ExpertBank):
         # a host read of the split sizes, like the reference. None picks p2p for bf16 on CUDA.
         self.transport = transport
         self._p2p = None
-        self._epoch = 0
         self._init_bank(self.num_local_experts, hidden_size, intermediate_size)
+        from prism_infer_b200 import ops
+        self.op_id = ops.ep_bank_id(self)   # names this bank to torch.ops.prism_moe.ep_forward
 
     # ------------------------------------------------------------------ NVLink peer transport
 
@@ -131,7 +132,6 @@ class ExpertParallelMoE(ExpertBank):
         self._p2p = dict(max_tokens=max_tokens, top_k=top_k, ptr=ptr, peers=peers,
                          table=torch.tensor(peers, dtype=torch.int64, device=dev),
                          ws=torch.zeros(ws_bytes, dtype=torch.uint8, device=dev))
-        self._epoch = 0
         if W > 1:
             dist.barrier(group=self.group)
 
@@ -154,7 +154,11 @@ class ExpertParallelMoE(ExpertBank):
                     top_k: int | None = None, renorm: bool = True) -> torch.Tensor:
         """One step over NVLink peer memory: route (from logits, or given ids/weights), dispatch
         into the owners' landing zones, grouped experts, outputs stored back into the sources'
-        landing zones by the down GEMM, combine. Collective over the EP group."""
+        landing zones by the down GEMM, combine. Collective over the EP group.
+
+        The step's epoch is counted on the device (epoch argument 0), so after the first call
+        (which reserves the landing zones, a collective that allocates) a step can be captured in
+        a CUDA graph and replayed; every rank must replay it the same number of times."""
         T = x.shape[0]
         k = top_k if top_k is not None else topk_ids.shape[1]
         if self._p2p is None or self._p2p["top_k"] != k:
@@ -163,7 +167,6 @@ class ExpertParallelMoE(ExpertBank):
         if T > st["max_tokens"]:
             raise RuntimeError(f"{T} tokens exceed the expert-parallel landing capacity "
                                f"{st['max_tokens']}; call reserve() with a larger max_tokens")
-        self._epoch += 1
         x = x.contiguous()
         out = torch.empty_like(x)
         ids = None if topk_ids is None else topk_ids.contiguous()
@@ -174,10 +177,25 @@ class ExpertParallelMoE(ExpertBank):
             x.data_ptr(), capi.ptr(lg), capi.ptr(ids), capi.ptr(w), capi.BF16, T,
             st["max_tokens"], self.hidden_size, self.intermediate_size, self.num_experts, k,
             int(bool(renorm)), self.ep_size, self.ep_rank, self.w_gate_up.data_ptr(),
-            self.w_down.data_ptr(), st["ptr"], st["table"].data_ptr(), self._epoch,
+            self.w_down.data_ptr(), st["ptr"], st["table"].data_ptr(), 0,
             out.data_ptr(), st["ws"].data_ptr(), st["ws"].numel(), capi.stream_of(x.device)),
             "prism_moe_ep_forward")
         return out
+
+    def step_stats(self) -> dict:
+        """Timing and row counts of the last step (``capi.ep_read_stats``; synchronises)."""
+        if self._p2p is None:
+            raise RuntimeError("no expert-parallel step has run")
+        return capi.ep_read_stats(self._p2p["ws"])
+
+    def landing_bytes(self) -> int:
+        """Bytes of this rank's landing zone (0 before the first step)."""
+        if self._p2p is None:
+            return 0
+        st = self._p2p
+        return int(capi.load().prism_moe_ep_landing_bytes(
+            self.ep_size, st["max_tokens"], st["top_k"], self.hidden_size, self.num_experts,
+            capi.BF16))
 
     def check_device_error(self) -> None:
         """Synchronise and raise if a kernel of the last step recorded an error (a peer wait

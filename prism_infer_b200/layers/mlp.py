@@ -14,7 +14,7 @@ from __future__ import annotations
 import torch
 from torch import nn
 
-from prism_infer_b200 import capi
+from prism_infer_b200 import ops  # noqa: F401  (registers torch.ops.prism_moe)
 
 
 class MergedGateUp(nn.Module):
@@ -84,6 +84,6 @@ class Qwen3MLP(nn.Module):
         wd = self.down_proj.weight
         if x2.dtype != wgu.dtype:
             raise RuntimeError(f"input dtype {x2.dtype} != MLP weight dtype {wgu.dtype}")
-        y = capi.expert_swiglu(x2, _one_segment(x2.shape[0], x2.device), wgu.unsqueeze(0),
-                               wd.unsqueeze(0))
+        y = torch.ops.prism_moe.expert_swiglu(x2, _one_segment(x2.shape[0], x2.device),
+                                              wgu.unsqueeze(0), wd.unsqueeze(0), None)
         return y.view(shape)

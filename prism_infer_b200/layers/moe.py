@@ -10,41 +10,27 @@ shape and dtype (moe.py:69-100). The expert-parallel size is read from the proce
 Forward, single GPU (EP=1):
   1. ``router_logits = F.linear(x, gate.weight)`` — the reference's own call (moe.py:74), so the
      logits are bit-identical to the reference's on the same device;
-  2. ``prism_moe_block_forward`` (C ABI): route (softmax/top-k/renorm, bit-exact with torch on
-     CUDA), dispatch plan, row permutation, grouped SwiGLU experts on tcgen05, weighted combine.
-No host synchronisation happens inside ``forward``; it can be captured in a CUDA graph.
+  2. ``torch.ops.prism_moe.block_forward`` (``prism_moe_block_forward`` in the C ABI): route
+     (softmax/top-k/renorm, bit-exact with torch on CUDA), dispatch plan, row permutation,
+     grouped SwiGLU experts on tcgen05, weighted combine. Under expert parallelism,
+     ``torch.ops.prism_moe.ep_forward`` runs the step over NVLink peer memory.
+No host synchronisation happens inside ``forward``; it can be captured in a CUDA graph (under
+expert parallelism after the first call, which reserves the landing zones), and it traces
+through ``torch.compile(fullgraph=True)`` (the ops have fake implementations).
 Only bfloat16 and float32 on an sm_100 device are supported; anything else raises.
 """
 from __future__ import annotations
-
-import threading
 
 import torch
 import torch.nn.functional as F
 from torch import nn
 
-from prism_infer_b200 import capi
+from prism_infer_b200 import capi, ops  # noqa: F401  (ops registers torch.ops.prism_moe)
 from prism_infer_b200.engine.parallel.expert_parallel import (
     ExpertParallelMoE,
     get_expert_parallel_size,
 )
 from prism_infer_b200.layers.experts import ExpertBank
-
-_ws_lock = threading.Lock()
-_workspaces: dict = {}
-
-
-def block_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """Per-(device, stream) scratch for ``prism_moe_block_forward``; grows on demand. The first
-    four bytes are the kernels' device error word (kept zero)."""
-    stream = torch.cuda.current_stream(device).cuda_stream
-    key = (device.index, stream)
-    with _ws_lock:
-        ws = _workspaces.get(key)
-        if ws is None or ws.numel() < nbytes:
-            ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
-            _workspaces[key] = ws
-    return ws
 
 
 class ReplicatedGate(nn.Module):
@@ -106,37 +92,30 @@ class MoE(ExpertBank):
         x = hidden_states.reshape(-1, orig_shape[-1])
         if not x.is_contiguous():
             x = x.contiguous()
-        T, H = x.shape
         if x.dtype != self.gate.weight.dtype:
             raise RuntimeError(f"hidden_states dtype {x.dtype} != MoE weight dtype "
                                f"{self.gate.weight.dtype}")
         logits = self.gate(x)                     # moe.py:74 — cuBLAS, as in the reference
         if self.ep_size > 1:
-            if self.ep_moe.use_p2p(x):
-                out = self.ep_moe.forward_p2p(x, router_logits=logits, top_k=self.top_k,
-                                              renorm=self.norm_topk_prob)
+            bank = self.ep_moe
+            if bank.use_p2p(x):
+                out = torch.ops.prism_moe.ep_forward(x, logits, bank.w_gate_up, bank.w_down,
+                                                     self.top_k, bool(self.norm_topk_prob),
+                                                     bank.op_id)
                 return out.view(orig_shape)
-            ids, w, _ = capi.route_topk(logits, self.top_k, self.norm_topk_prob)
-            return self.ep_moe(x, ids, w).view(orig_shape)
-        out = torch.empty_like(x)
-        if T == 0:
-            return out.view(orig_shape)
-        lib = capi.load()
-        dt = capi.dtype_code(x.dtype)
-        nbytes = lib.prism_moe_block_workspace_size(T, H, self.intermediate_size,
-                                                    self.num_experts, self.top_k, dt)
-        ws = block_workspace(x.device, nbytes)
-        capi.check(lib.prism_moe_block_forward(
-            x.data_ptr(), logits.data_ptr(), dt, T, H, self.intermediate_size, self.num_experts,
-            self.top_k, int(bool(self.norm_topk_prob)), self.w_gate_up.data_ptr(),
-            self.w_down.data_ptr(), out.data_ptr(), None, None, ws.data_ptr(), ws.numel(),
-            capi.stream_of(x.device)), "prism_moe_block_forward")
+            ids, w = torch.ops.prism_moe.route_topk(logits, self.top_k,
+                                                    bool(self.norm_topk_prob))
+            return bank(x, ids, w).view(orig_shape)
+        out = torch.ops.prism_moe.block_forward(x, logits, self.w_gate_up, self.w_down,
+                                                self.top_k, bool(self.norm_topk_prob))
         return out.view(orig_shape)
 
     def check_device_error(self, device=None) -> None:
         """Synchronise and raise if a kernel of the last forward recorded an error."""
+        if self.ep_moe is not None:
+            self.ep_moe.check_device_error()
+            return
         dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
-        stream = torch.cuda.current_stream(dev).cuda_stream
-        ws = _workspaces.get((dev.index, stream))
-        if ws is not None:
-            capi.check(capi.read_device_error(ws[:4].view(torch.int32), dev), "MoE kernels")
+        word = capi.block_error_word(dev)
+        if word is not None:
+            capi.check(capi.read_device_error(word, dev), "MoE kernels")

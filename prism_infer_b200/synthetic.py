@@ -139,10 +139,19 @@ def make_weights_torch(H: int, E: int, I: int, seed: int, dtype, device, skew: b
     gu = torch.empty(hi - lo, 2 * I, H, device=device, dtype=dtype)
     dn = torch.empty(hi - lo, H, I, device=device, dtype=dtype)
     for e in range(lo, hi):
-        g.manual_seed(seed * 1009 + e)
-        gu[e - lo] = (torch.randn(2 * I, H, generator=g, device=device) / math.sqrt(H)).to(dtype)
-        dn[e - lo] = (torch.randn(H, I, generator=g, device=device) / math.sqrt(I)).to(dtype)
+        gu[e - lo], dn[e - lo] = expert_weights_torch(H, I, seed, e, dtype, device)
     return w_gate.to(dtype), gu, dn
+
+
+def expert_weights_torch(H: int, I: int, seed: int, e: int, dtype, device):
+    """Expert ``e``'s (w_gate_up [2I,H], w_down [H,I]) exactly as ``make_weights_torch`` draws
+    them (its own generator, seeded ``seed*1009 + e``)."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 1009 + e)
+    gu = (torch.randn(2 * I, H, generator=g, device=device) / math.sqrt(H)).to(dtype)
+    dn = (torch.randn(H, I, generator=g, device=device) / math.sqrt(I)).to(dtype)
+    return gu, dn
 
 
 def make_hidden_torch(T: int, H: int, seed: int, dtype, device, skew: bool = False):

@@ -29,6 +29,14 @@ def _seed():
     torch.manual_seed(0)
 
 
+@pytest.fixture
+def expert_engine():
+    """Select the library's expert GEMM engine for one test (``auto`` again afterwards)."""
+    from prism_infer_b200 import capi
+    yield capi.set_expert_engine
+    capi.set_expert_engine("auto")
+
+
 def load_golden(name):
     import numpy as np
     return dict(np.load(GOLDEN / f"{name}.npz", allow_pickle=False))

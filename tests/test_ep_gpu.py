@@ -20,7 +20,7 @@ REPO = Path(__file__).resolve().parent.parent
 BF16_MAX_ABS, BF16_MEAN_REL = 2e-2, 1e-2
 
 
-def _worker(rank, W, port, case, outdir, transport):
+def _worker(rank, W, port, case, outdir, transport, skew=False, sample=0):
     sys.path.insert(0, str(REPO))
     from datetime import timedelta
 
@@ -37,16 +37,17 @@ def _worker(rank, W, port, case, outdir, transport):
                             device_id=dev)
     H, E, k, I, Ts, seed = case
     set_expert_parallel_size(W)
-    wts = synthetic.make_weights_np(H, E, I, seed)
     El = E // W
+    wts = synthetic.make_weights_np(H, E, I, seed, skew=skew, k=k,
+                                    experts=slice(rank * El, (rank + 1) * El))
     moe = MoE(H, I, E, k)
     with torch.no_grad():
         moe.gate.weight.copy_(torch.from_numpy(wts.w_gate))
-        moe.ep_moe.w_gate_up.copy_(torch.from_numpy(wts.w_gate_up[rank * El:(rank + 1) * El]))
-        moe.ep_moe.w_down.copy_(torch.from_numpy(wts.w_down[rank * El:(rank + 1) * El]))
+        moe.ep_moe.w_gate_up.copy_(torch.from_numpy(wts.w_gate_up))
+        moe.ep_moe.w_down.copy_(torch.from_numpy(wts.w_down))
     moe = moe.to(dev, torch.bfloat16)
     moe.ep_moe.transport = transport
-    x = synthetic.make_hidden_np(Ts[rank], H, seed + 100 * (rank + 1))
+    x = synthetic.make_hidden_np(Ts[rank], H, seed + 100 * (rank + 1), skew=skew)
     xt = torch.from_numpy(x).to(dev, torch.bfloat16)
     with torch.inference_mode():
         logits, ids, _ = moe.route(xt)
@@ -57,9 +58,11 @@ def _worker(rank, W, port, case, outdir, transport):
     if transport == "p2p":
         moe.ep_moe.check_device_error()
         assert torch.equal(out2, out3)
-    np.savez(Path(outdir) / f"r{rank}.npz", x=x, logits=logits.float().cpu().numpy(),
-             ids=ids.cpu().numpy(), out=out.float().cpu().numpy(),
-             out2=out2.float().cpu().numpy())
+    rows = (np.linspace(0, Ts[rank] - 1, sample).round().astype(np.int64) if sample
+            else np.arange(Ts[rank]))
+    np.savez(Path(outdir) / f"r{rank}.npz", x=x[rows], rows=rows,
+             logits=logits.float().cpu().numpy(), ids=ids.cpu().numpy(),
+             out=out.float().cpu().numpy()[rows], out2=out2.float().cpu().numpy()[rows])
     dist.barrier()
     dist.destroy_process_group()
 
@@ -100,6 +103,49 @@ def test_ep_matches_oracle(W, case, transport):
         assert res[r]["out"].shape == ref.shape
         if ref.size == 0:            # a rank with no tokens still takes part in the exchange
             continue
+        d = np.abs(res[r]["out"] - ref)
+        assert d.max() <= BF16_MAX_ABS, (r, d.max())
+        assert d.mean() / np.abs(ref).mean() <= BF16_MEAN_REL
+        assert np.array_equal(res[r]["out"], res[r]["out2"])
+
+
+FULL_CASES = [
+    ((2048, 128, 8, 768, (8192,) * 8, 2000), False),    # benchmark config 2: T=8192 per rank
+    ((2048, 128, 8, 768, (4096,) * 8, 3000), True),     # config 3: Zipf-skewed routing
+]
+
+
+@pytest.mark.parametrize("W", [2, 8])
+@pytest.mark.parametrize("case,skew", FULL_CASES, ids=["cfg2_T8192", "cfg3_skew_T4096"])
+def test_ep_full_size(W, case, skew):
+    """Full benchmark sizes over the NVLink transport: every token's routing bit-exact against
+    the oracle on the same logits, 48 tokens per rank against the oracle's expert math (a
+    token's output depends only on its own row, its routing and the experts' weights)."""
+    if torch.cuda.device_count() < W:
+        pytest.skip(f"needs {W} GPUs")
+    import torch.multiprocessing as mp
+
+    from oracle import moe_oracle as O
+    from prism_infer_b200 import synthetic
+    H, E, k, I, Ts, seed = case
+    Ts = Ts[:W]
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_worker, args=(W, port, (H, E, k, I, Ts, seed), d, "p2p", skew, 48),
+                           nprocs=W, join=True, start_method="spawn")
+        res = [dict(np.load(Path(d) / f"r{r}.npz")) for r in range(W)]
+    wts = synthetic.make_weights_np(H, E, I, seed, skew=skew, k=k)
+    for r in range(W):
+        ids, w = O.route(res[r]["logits"], k, True, "bfloat16")
+        assert (res[r]["ids"] == ids).all(), r
+        rows = res[r]["rows"]
+        xs = O.bf16_round(res[r]["x"])
+        ys = np.stack([np.stack([O.expert_mlp(xs[i:i + 1], O.bf16_round(wts.w_gate_up[e]),
+                                               O.bf16_round(wts.w_down[e]), "bfloat16")[0]
+                                 for e in ids[t]]) for i, t in enumerate(rows)])
+        ref = O.combine_weighted_sum(ys.reshape(-1, H), w[rows], len(rows), k, "bfloat16")
         d = np.abs(res[r]["out"] - ref)
         assert d.max() <= BF16_MAX_ABS, (r, d.max())
         assert d.mean() / np.abs(ref).mean() <= BF16_MEAN_REL

@@ -172,7 +172,7 @@ def _segments(counts, device=DEV):
 ])
 @pytest.mark.parametrize("dtype,engine", [(torch.bfloat16, "fused"), (torch.bfloat16, "single"),
                                           (torch.bfloat16, "pair"), (torch.float32, "simt")])
-def test_expert_swiglu_matches_oracle(H, I, counts, dtype, engine, monkeypatch):
+def test_expert_swiglu_matches_oracle(H, I, counts, dtype, engine, expert_engine):
     """``engine``: bf16 tcgen05 with both GEMMs in one persistent launch (128-row tiles), two
     launches of single-CTA tiles (128 rows), or two launches of CTA-pair tiles (256 rows,
     cta_group::2); fp32 runs on CUDA cores."""
@@ -181,7 +181,7 @@ def test_expert_swiglu_matches_oracle(H, I, counts, dtype, engine, monkeypatch):
     if dtype == torch.float32 and sum(counts) > 5000:
         pytest.skip("fp32 CUDA-core path is exercised at the smaller row counts")
     if dtype == torch.bfloat16:
-        monkeypatch.setenv("PRISM_MOE_GEMM_ENGINE", engine)
+        expert_engine(engine)
     gen = torch.Generator(device=DEV).manual_seed(H + I + len(counts))
     E = len(counts)
     R = int(sum(counts))
@@ -212,9 +212,9 @@ def test_expert_swiglu_matches_oracle(H, I, counts, dtype, engine, monkeypatch):
 
 
 @pytest.mark.parametrize("engine", ["fused", "single", "pair"])
-def test_expert_swiglu_segment_expert_map(engine, monkeypatch):
+def test_expert_swiglu_segment_expert_map(engine, expert_engine):
     """Segments may name any local expert (EP receiver layout: (source rank, local expert))."""
-    monkeypatch.setenv("PRISM_MOE_GEMM_ENGINE", engine)
+    expert_engine(engine)
     H, I, El = 256, 128, 3
     x = torch.randn(300, H, device=DEV).to(torch.bfloat16)
     wgu = (torch.randn(El, 2 * I, H, device=DEV) / 16).to(torch.bfloat16)
