@@ -327,6 +327,7 @@ def parity_check(moe, x, cfg_id, world, rank, device, n_sample=32):
         "mean_rel": vals[3] / max(vals[4], 1e-30), "device_error_ranks": int(vals[5]),
         "tolerance": {"max_abs": PARITY_MAX_ABS, "mean_rel": PARITY_MEAN_REL},
         "max_expert_load_over_mean": max(load) / mean_load if mean_load else None,
+        "ref_mean_abs": vals[4] / max(reduce_over_ranks([float(ref.numel())], "sum", world)[0], 1),
     }
     res["ok"] = bool(res["ids_exact"] and res["weights_exact"] and res["device_error_ranks"] == 0
                      and res["max_abs"] <= PARITY_MAX_ABS

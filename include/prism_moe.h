@@ -172,6 +172,37 @@ int prism_moe_combine(const void* expert_out, int dtype, const int32_t* entry_ro
                       const void* topk_weights, int64_t num_tokens, int32_t top_k, int64_t hidden,
                       void* out, void* stream);
 
+/*
+ * RMSNorm of [T, H] rows, optionally after adding the residual stream — the decoder layer's
+ * norms, replacing prism_infer/layers/layernorm.py:16-40 (rms_forward when ``residual`` is NULL,
+ * else add_rms_forward). Numerics as the reference: xf = float(x) (+ float(residual)),
+ * residual_out = dtype(xf), out = dtype(dtype(xf * rsqrt(mean(xf^2) + eps)) * weight); the
+ * reference compiles these with torch.compile, so sums of squares agree to rounding, not bits.
+ *   x, residual, out, residual_out [T, H], weight [H]: dtype, 16-byte aligned rows.
+ * ``out`` may be ``x`` or ``residual``; ``residual_out`` (required with a residual) may not.
+ * One warp per row.
+ */
+int prism_moe_rmsnorm(const void* x, const void* residual, const void* weight, float eps,
+                      int dtype, int64_t num_tokens, int64_t hidden, void* out,
+                      void* residual_out, void* stream);
+
+/*
+ * The decoder layer's next residual add and RMSNorm, applied to the block output inside the
+ * combine kernel (prism_infer/models/qwen3.py:179-186 runs them as the next layer's
+ * input_layernorm(hidden, residual), layernorm.py:28-40): the *_norm entry points write
+ *   residual_out = dtype(float(block output) + float(residual))
+ *   out          = RMSNorm(that sum) with norm_weight and eps
+ * instead of the block output, bit for bit what the plain entry point followed by
+ * prism_moe_rmsnorm(out, residual, ...) gives, without the block output's round trip through
+ * HBM. ``residual_out`` may alias neither ``residual`` nor ``out``.
+ */
+typedef struct prism_moe_norm_epilogue {
+  const void* residual;      /* [T, H] dtype */
+  const void* norm_weight;   /* [H] dtype    */
+  float eps;
+  void* residual_out;        /* [T, H] dtype */
+} prism_moe_norm_epilogue;
+
 /* Bytes of scratch prism_moe_block_forward needs. */
 size_t prism_moe_block_workspace_size(int64_t num_tokens, int64_t hidden, int64_t inter,
                                       int32_t num_experts, int32_t top_k, int dtype);
@@ -192,6 +223,16 @@ int prism_moe_block_forward(const void* x, const void* router_logits, int dtype,
                             const void* w_gate_up, const void* w_down, void* out,
                             int64_t* topk_ids, void* topk_weights, void* workspace,
                             size_t workspace_bytes, void* stream);
+
+/* prism_moe_block_forward with the decoder layer's residual add + RMSNorm fused into the
+ * combine (``epilogue`` NULL: identical to prism_moe_block_forward). */
+int prism_moe_block_forward_norm(const void* x, const void* router_logits, int dtype,
+                                 int64_t num_tokens, int64_t hidden, int64_t inter,
+                                 int32_t num_experts, int32_t top_k, int32_t renorm,
+                                 const void* w_gate_up, const void* w_down, void* out,
+                                 int64_t* topk_ids, void* topk_weights, void* workspace,
+                                 size_t workspace_bytes, void* stream,
+                                 const prism_moe_norm_epilogue* epilogue);
 
 /* ---------------------------------------------------------------------------------------------
  * Expert parallelism over NVLink peer memory (one process per GPU).
@@ -253,6 +294,17 @@ int prism_moe_ep_forward(const void* x, const void* router_logits, const int64_t
                          const void* w_gate_up, const void* w_down, void* my_landing,
                          const uint64_t* peer_landing, uint64_t epoch, void* out,
                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* prism_moe_ep_forward with the decoder layer's residual add + RMSNorm fused into the final
+ * combine (``epilogue`` NULL: identical to prism_moe_ep_forward). */
+int prism_moe_ep_forward_norm(const void* x, const void* router_logits, const int64_t* topk_ids,
+                              const void* topk_weights, int dtype, int64_t num_tokens,
+                              int64_t max_tokens, int64_t hidden, int64_t inter,
+                              int32_t num_experts, int32_t top_k, int32_t renorm,
+                              int32_t ep_size, int32_t ep_rank, const void* w_gate_up,
+                              const void* w_down, void* my_landing, const uint64_t* peer_landing,
+                              uint64_t epoch, void* out, void* workspace, size_t workspace_bytes,
+                              void* stream, const prism_moe_norm_epilogue* epilogue);
 
 /*
  * Statistics of the last prism_moe_ep_forward step that used ``workspace`` (synchronises

@@ -8,6 +8,8 @@ This module restates, in numpy, the algorithm of the reference's MoE hot path:
 * ``build_dispatch_plan``         prism_infer/engine/parallel/expert_parallel.py:23-42
 * ``combine_weighted_sum``        prism_infer/engine/parallel/expert_parallel.py:45-57
 * ``ExpertParallelMoE.forward``   prism_infer/engine/parallel/expert_parallel.py:140-176
+* ``RMSNorm.rms_forward`` / ``add_rms_forward``   prism_infer/layers/layernorm.py:16-40 (the
+  decoder layer's norms at the block's edges, prism_infer/models/qwen3.py:179-186)
 
 It is the checker, never the thing measured or shipped: only ``tests/``,
 ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg may import it. The product
@@ -41,7 +43,7 @@ import numpy as np
 __all__ = [
     "bf16_round", "router_logits", "softmax_fp32", "topk_torch_cuda", "renorm_weights", "route",
     "expert_mlp", "moe_forward", "build_dispatch_plan", "combine_weighted_sum",
-    "ep_forward_all_ranks", "expert_major_order", "expert_counts",
+    "ep_forward_all_ranks", "expert_major_order", "expert_counts", "rms_norm",
 ]
 
 
@@ -384,3 +386,28 @@ def ep_forward_all_ranks(xs: list, w_gate: np.ndarray, w_gate_up: np.ndarray,
         T = ranks[r]["x"].shape[0]
         ranks[r]["out"] = combine_weighted_sum(unperm, ranks[r]["topk_weights"], T, k, dtype)
     return ranks
+
+
+# ----------------------------------------------------------------------------------------
+# Decoder-layer norms at the block's edges (layernorm.py:16-40)
+# ----------------------------------------------------------------------------------------
+
+def rms_norm(x: np.ndarray, weight: np.ndarray, eps: float, dtype: str,
+             residual: np.ndarray | None = None):
+    """``RMSNorm.rms_forward(x)`` (layernorm.py:16-26) or, with ``residual``,
+    ``add_rms_forward(x, residual)`` (:28-40), which returns ``(out, residual_out)``.
+
+    xf = float(x) (+ float(residual)); residual_out = dtype(xf); var = mean(xf^2);
+    out = dtype(dtype(xf * rsqrt(var + eps)) * weight) — the product with the weight is a
+    ``dtype`` multiply (one rounding). The mean's summation order is numpy's, so the result
+    agrees with the reference to rounding, not bit for bit.
+    """
+    xf = _cast(x, dtype).astype(np.float32)
+    if residual is not None:
+        xf = (xf + _cast(residual, dtype).astype(np.float32)).astype(np.float32)
+    res_out = _cast(xf, dtype)
+    var = np.mean(xf * xf, axis=-1, keepdims=True, dtype=np.float32)
+    rs = (np.float32(1.0) / np.sqrt(var + np.float32(eps))).astype(np.float32)
+    n = _cast((xf * rs).astype(np.float32), dtype)
+    out = _cast((n * _cast(weight, dtype)).astype(np.float32), dtype)
+    return out if residual is None else (out, res_out)

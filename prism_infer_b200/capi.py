@@ -24,6 +24,16 @@ EP_STATS_FIELDS = ("epoch", "counter", "dispatch_t0_ns", "dispatch_t1_ns", "fuse
                    "fused_t1_ns", "send_rows", "recv_rows")
 
 _vp, _i32, _i64, _sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t
+
+
+class NormEpilogue(ctypes.Structure):
+    """``prism_moe_norm_epilogue``: the decoder layer's residual add + RMSNorm fused into the
+    block's combine."""
+    _fields_ = [("residual", ctypes.c_void_p), ("norm_weight", ctypes.c_void_p),
+                ("eps", ctypes.c_float), ("residual_out", ctypes.c_void_p)]
+
+
+_ep = ctypes.POINTER(NormEpilogue)
 _SIGNATURES = {
     "prism_moe_version": (ctypes.c_int, []),
     "prism_moe_last_error": (ctypes.c_char_p, []),
@@ -58,6 +68,15 @@ _SIGNATURES = {
     "prism_moe_ep_read_stats": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_uint64), _vp]),
     "prism_moe_set_expert_engine": (ctypes.c_int, [ctypes.c_int]),
     "prism_moe_set_wait_limits": (ctypes.c_int, [_i64, _i64]),
+    "prism_moe_rmsnorm": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_float, ctypes.c_int, _i64, _i64,
+                                         _vp, _vp, _vp]),
+    "prism_moe_block_forward_norm": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _i64, _i64, _i64, _i32,
+                                                    _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
+                                                    _vp, _ep]),
+    "prism_moe_ep_forward_norm": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, _i64, _i64,
+                                                 _i64, _i64, _i32, _i32, _i32, _i32, _i32, _vp,
+                                                 _vp, _vp, _vp, ctypes.c_uint64, _vp, _vp, _sz,
+                                                 _vp, _ep]),
     "prism_moe_profile_events": (ctypes.c_int, [ctypes.POINTER(_vp), _i32]),
     "prism_moe_read_device_error": (ctypes.c_int, [_vp, _vp]),
 }
@@ -254,10 +273,39 @@ def block_error_word(device):
     return None if ws is None else ws[:4].view(torch.int32)
 
 
-def block_forward(x, router_logits, w_gate_up, w_down, top_k: int, renorm: bool, out=None):
+def norm_epilogue(residual, norm_weight, eps: float, residual_out):
+    """A ``prism_moe_norm_epilogue`` for the *_norm entry points (None when ``norm_weight`` is
+    None). The tensors must stay alive for the call."""
+    if norm_weight is None:
+        return None
+    _need_cuda(residual, norm_weight, residual_out)
+    return NormEpilogue(residual.data_ptr(), norm_weight.data_ptr(), float(eps),
+                        residual_out.data_ptr())
+
+
+def rmsnorm(x, weight, eps: float, residual=None):
+    """RMSNorm of ``x`` [T,H] (prism_moe_rmsnorm); with ``residual``, of ``x + residual``, and
+    returns (out, residual_out) as the reference's add_rms_forward does."""
+    torch = _torch()
+    _need_cuda(x, weight, residual)
+    T, H = x.shape
+    if weight.shape != (H,) or weight.dtype != x.dtype or (
+            residual is not None and (residual.shape != x.shape or residual.dtype != x.dtype)):
+        raise RuntimeError("rmsnorm: inconsistent shapes or dtypes")
+    out = torch.empty_like(x)
+    res_out = torch.empty_like(x) if residual is not None else None
+    check(load().prism_moe_rmsnorm(ptr(x), ptr(residual), ptr(weight), float(eps),
+                                   dtype_code(x.dtype), T, H, ptr(out), ptr(res_out),
+                                   stream_of(x.device)), "prism_moe_rmsnorm")
+    return out if residual is None else (out, res_out)
+
+
+def block_forward(x, router_logits, w_gate_up, w_down, top_k: int, renorm: bool, out=None,
+                  epilogue=None):
     """The single-GPU block after the router GEMM (prism_moe_block_forward): route, plan,
     gather, grouped SwiGLU experts, combine. ``x`` [T,H], ``router_logits`` [T,E],
-    ``w_gate_up`` [E,2I,H], ``w_down`` [E,H,I]; returns [T,H]."""
+    ``w_gate_up`` [E,2I,H], ``w_down`` [E,H,I]; returns [T,H]. ``epilogue`` (a NormEpilogue)
+    fuses the decoder layer's next residual add + RMSNorm into the combine."""
     torch = _torch()
     _need_cuda(x, router_logits, w_gate_up, w_down)
     T, H = x.shape
@@ -276,9 +324,10 @@ def block_forward(x, router_logits, w_gate_up, w_down, top_k: int, renorm: bool,
     dt = dtype_code(x.dtype)
     nbytes = lib.prism_moe_block_workspace_size(T, H, I, E, top_k, dt)
     ws = block_workspace(x.device, nbytes)
-    check(lib.prism_moe_block_forward(
+    check(lib.prism_moe_block_forward_norm(
         ptr(x), ptr(router_logits), dt, T, H, I, E, top_k, int(bool(renorm)), ptr(w_gate_up),
-        ptr(w_down), ptr(out), None, None, ptr(ws), ws.numel(), stream_of(x.device)),
+        ptr(w_down), ptr(out), None, None, ptr(ws), ws.numel(), stream_of(x.device),
+        ctypes.byref(epilogue) if epilogue is not None else None),
         "prism_moe_block_forward")
     return out
 

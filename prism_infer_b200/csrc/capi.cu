@@ -227,12 +227,13 @@ size_t prism_moe_block_workspace_size(int64_t num_tokens, int64_t hidden, int64_
   return block_layout(num_tokens, hidden, inter, num_experts, top_k, dtype).total;
 }
 
-int prism_moe_block_forward(const void* x, const void* router_logits, int dtype,
-                            int64_t num_tokens, int64_t hidden, int64_t inter,
-                            int32_t num_experts, int32_t top_k, int32_t renorm,
-                            const void* w_gate_up, const void* w_down, void* out,
-                            int64_t* topk_ids, void* topk_weights, void* workspace,
-                            size_t workspace_bytes, void* stream) {
+int prism_moe_block_forward_norm(const void* x, const void* router_logits, int dtype,
+                                 int64_t num_tokens, int64_t hidden, int64_t inter,
+                                 int32_t num_experts, int32_t top_k, int32_t renorm,
+                                 const void* w_gate_up, const void* w_down, void* out,
+                                 int64_t* topk_ids, void* topk_weights, void* workspace,
+                                 size_t workspace_bytes, void* stream,
+                                 const prism_moe_norm_epilogue* epilogue) {
   PRISM_CHECK_ARG(dtype_ok(dtype), "block_forward: unknown dtype %d", dtype);
   PRISM_CHECK_ARG(num_tokens >= 0 && hidden >= 1 && inter >= 1, "block_forward: bad shape");
   PRISM_CHECK_ARG(num_experts >= 1 && num_experts <= 1024, "block_forward: num_experts %d outside [1, 1024]",
@@ -244,6 +245,9 @@ int prism_moe_block_forward(const void* x, const void* router_logits, int dtype,
                   "block_forward: workspace too small (%zu < %zu)", workspace_bytes, L.total);
   PRISM_CHECK_ARG(num_tokens == 0 || (x && router_logits && w_gate_up && w_down && out),
                   "block_forward: null pointer");
+  PRISM_CHECK_ARG(!epilogue || (epilogue->residual && epilogue->norm_weight &&
+                                epilogue->residual_out && epilogue->eps >= 0.f),
+                  "block_forward: incomplete norm epilogue");
   if (int r = check_device()) return r;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (num_tokens == 0) return PRISM_MOE_OK;
@@ -277,9 +281,44 @@ int prism_moe_block_forward(const void* x, const void* router_logits, int dtype,
                           static_cast<const float*>(w_down), static_cast<float*>(y),
                           static_cast<float*>(h), st);
   if (r) return r;
-  r = combine(y, dtype, entry_row, w, num_tokens, top_k, hidden, out, st);
+  CombineSource src{};
+  if (epilogue) {
+    src.residual = epilogue->residual;
+    src.norm_weight = epilogue->norm_weight;
+    src.residual_out = epilogue->residual_out;
+    src.eps = epilogue->eps;
+  }
+  r = combine(y, dtype, entry_row, w, num_tokens, top_k, hidden, out, st, &src);
   record_stage(6, st);
   return r;
+}
+
+int prism_moe_block_forward(const void* x, const void* router_logits, int dtype,
+                            int64_t num_tokens, int64_t hidden, int64_t inter,
+                            int32_t num_experts, int32_t top_k, int32_t renorm,
+                            const void* w_gate_up, const void* w_down, void* out,
+                            int64_t* topk_ids, void* topk_weights, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  return prism_moe_block_forward_norm(x, router_logits, dtype, num_tokens, hidden, inter,
+                                      num_experts, top_k, renorm, w_gate_up, w_down, out,
+                                      topk_ids, topk_weights, workspace, workspace_bytes, stream,
+                                      nullptr);
+}
+
+int prism_moe_rmsnorm(const void* x, const void* residual, const void* weight, float eps,
+                      int dtype, int64_t num_tokens, int64_t hidden, void* out,
+                      void* residual_out, void* stream) {
+  PRISM_CHECK_ARG(dtype_ok(dtype), "rmsnorm: unknown dtype %d", dtype);
+  PRISM_CHECK_ARG(num_tokens >= 0 && hidden >= 1, "rmsnorm: bad shape");
+  PRISM_CHECK_ARG(eps >= 0.f, "rmsnorm: negative eps");
+  PRISM_CHECK_ARG(num_tokens == 0 || (x && weight && out), "rmsnorm: null pointer");
+  PRISM_CHECK_ARG((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(residual) |
+                   reinterpret_cast<uintptr_t>(weight) | reinterpret_cast<uintptr_t>(out) |
+                   reinterpret_cast<uintptr_t>(residual_out)) % 16 == 0,
+                  "rmsnorm: buffers must be 16-byte aligned");
+  if (int r = check_device()) return r;
+  return rmsnorm(x, residual, weight, eps, dtype, num_tokens, hidden, out, residual_out,
+                 static_cast<cudaStream_t>(stream));
 }
 
 int prism_moe_profile_events(void* const* events, int32_t count) {

@@ -6,8 +6,16 @@
 // (or 4 fp32) columns per step and issues all k row loads before accumulating. k is a template
 // parameter for the common top-k values (rows and weights stay in registers); other k use a
 // generic loop.
+//
+// Optional epilogue (CombineSource::norm_weight): the decoder layer's next residual add and
+// RMSNorm on the block output, as prism_infer/models/qwen3.py:179-186 applies them in the next
+// layer (add_rms_forward, layernorm.py:28-40): residual_out = dtype(float(moe_out) + residual),
+// out = RMSNorm(that sum). The first pass writes moe_out into ``out`` and the residual, the
+// second re-reads both (the same lane's own writes) and overwrites ``out`` with the normalised
+// row — the arithmetic of norm.cuh, so it equals combine followed by prism_moe_rmsnorm.
 #include "common.cuh"
 #include "internal.h"
+#include "norm.cuh"
 
 namespace prism {
 namespace {
@@ -28,7 +36,7 @@ __device__ __forceinline__ void accumulate(float* acc, const uint4& u, float w) 
 }
 
 template <bool kBf16>
-__device__ __forceinline__ uint4 pack(const float* acc) {
+__device__ __forceinline__ uint4 pack(const float* acc) {   // round each sum once
   uint4 o;
   uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
   if constexpr (kBf16) {
@@ -54,7 +62,7 @@ template <bool kBf16, int kK>
 __global__ void __launch_bounds__(256)
     combine_kernel(const uint4* __restrict__ y, const int32_t* __restrict__ entry_row,
                    const void* __restrict__ w, int64_t T, int k_rt, int64_t vpr,
-                   uint4* __restrict__ out, CombineSource src) {
+                   uint4* out, CombineSource src) {
   constexpr int kEl = kBf16 ? 8 : 4;
   const int lane = threadIdx.x & 31;
   const int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -62,6 +70,21 @@ __global__ void __launch_bounds__(256)
   if (src.gate_err && *reinterpret_cast<const volatile int*>(src.gate_err) == PRISM_MOE_ERR_TIMEOUT)
     return;   // the step's exchange did not complete: its rows are not all there
   if (src.parity) y += static_cast<int64_t>(*src.parity & 1u) * (src.parity_stride_bytes / 16);
+  const bool norm = src.norm_weight != nullptr;
+  const uint4* res = static_cast<const uint4*>(src.residual);
+  uint4* res_out = static_cast<uint4*>(src.residual_out);
+  float ss = 0.f;
+  // one output vector: plain, or the first pass of the norm epilogue
+  auto emit = [&](int64_t v, const float* acc) {
+    const uint4 a = pack<kBf16>(acc);
+    out[t * vpr + v] = a;
+    if (norm) {
+      float xf[kEl];
+      const uint4 rv = res[t * vpr + v];
+      norm_sum<kBf16>(a, &rv, xf, ss);
+      res_out[t * vpr + v] = pack_vec<kBf16>(xf);
+    }
+  };
   const int k = kK > 0 ? kK : k_rt;
   // lane j < k fetches slot j's row and weight once; broadcast by shuffle
   int64_t my_row = -1;
@@ -89,7 +112,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
       for (int j = 0; j < kK; ++j)
         if (rows[j] >= 0) accumulate<kBf16>(acc, u[j], wt[j]);
-      out[t * vpr + v] = pack<kBf16>(acc);
+      emit(v, acc);
     }
   } else {
     for (int64_t v = lane; v < vpr; v += 32) {
@@ -101,7 +124,18 @@ __global__ void __launch_bounds__(256)
         const float wj = __shfl_sync(0xffffffffu, my_w, j);
         if (r >= 0) accumulate<kBf16>(acc, y[r * vpr + v], wj);
       }
-      out[t * vpr + v] = pack<kBf16>(acc);
+      emit(v, acc);
+    }
+  }
+  if (norm) {   // second pass: the normalised row
+    const float rs = rms_scale(warp_sum(ss), src.hidden, src.eps);
+    const uint4* wv = static_cast<const uint4*>(src.norm_weight);
+    for (int64_t v = lane; v < vpr; v += 32) {
+      float xf[kEl];
+      const uint4 rv = res[t * vpr + v];
+      float unused = 0.f;
+      norm_sum<kBf16>(out[t * vpr + v], &rv, xf, unused);
+      out[t * vpr + v] = norm_scale<kBf16>(xf, wv[v], rs);
     }
   }
 }
@@ -129,10 +163,15 @@ int combine(const void* y, int dtype, const int32_t* entry_row, const void* w, i
   PRISM_CHECK_ARG((hidden * el) % 16 == 0, "combine: hidden*elem_size must be a multiple of 16");
   PRISM_CHECK_ARG(k >= 1 && k <= 32, "combine: top_k %d outside [1, 32]", k);
   PRISM_CHECK_ARG(!src || src->parity_stride_bytes % 16 == 0, "combine: parity stride alignment");
+  PRISM_CHECK_ARG(!src || !src->norm_weight || (src->residual && src->residual_out),
+                  "combine: the norm epilogue needs residual and residual_out");
+  PRISM_CHECK_ARG(!src || !src->norm_weight ||
+                      (src->residual_out != src->residual && src->residual_out != out),
+                  "combine: residual_out must not alias residual or out");
   if (T == 0) return PRISM_MOE_OK;
   const int64_t vpr = hidden * el / 16;
-  const CombineSource plain{};
-  const CombineSource& s = src ? *src : plain;
+  CombineSource s = src ? *src : CombineSource{};
+  s.hidden = hidden;
   if (dtype == PRISM_MOE_BF16)
     launch_combine<true>(y, entry_row, w, T, k, vpr, out, s, st);
   else

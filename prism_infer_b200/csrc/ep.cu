@@ -389,13 +389,13 @@ __attribute__((visibility("default"))) size_t prism_moe_ep_workspace_size(
   return ep_ws_layout(max_tokens, hidden, inter, num_experts, top_k, ep_size, L.rcap, es).total;
 }
 
-__attribute__((visibility("default"))) int prism_moe_ep_forward(
+__attribute__((visibility("default"))) int prism_moe_ep_forward_norm(
     const void* x, const void* router_logits, const int64_t* topk_ids_in,
     const void* topk_weights_in, int dtype, int64_t num_tokens, int64_t max_tokens,
     int64_t hidden, int64_t inter, int32_t num_experts, int32_t top_k, int32_t renorm,
     int32_t ep_size, int32_t ep_rank, const void* w_gate_up, const void* w_down,
     void* my_landing, const uint64_t* peer_landing, uint64_t epoch, void* out, void* workspace,
-    size_t workspace_bytes, void* stream) {
+    size_t workspace_bytes, void* stream, const prism_moe_norm_epilogue* epilogue) {
   PRISM_CHECK_ARG(dtype == PRISM_MOE_BF16, "ep_forward: bf16 only");
   PRISM_CHECK_ARG(ep_size >= 1 && ep_size <= kMaxRanks && ep_rank >= 0 && ep_rank < ep_size,
                   "ep_forward: bad ep_size/ep_rank");
@@ -411,6 +411,9 @@ __attribute__((visibility("default"))) int prism_moe_ep_forward(
                       (num_tokens == 0 || (x && out)),
                   "ep_forward: null pointer");
   PRISM_CHECK_ARG(hidden % 8 == 0 && inter % 8 == 0, "ep_forward: hidden, inter % 8 != 0");
+  PRISM_CHECK_ARG(!epilogue || (epilogue->residual && epilogue->norm_weight &&
+                                epilogue->residual_out && epilogue->eps >= 0.f),
+                  "ep_forward: incomplete norm epilogue");
   const int64_t es = 2;
   const int W = ep_size, me = ep_rank, E = num_experts, El = E / W, k = top_k;
   const Landing LL = landing_layout(W, max_tokens, k, hidden, E, es);
@@ -522,9 +525,29 @@ __attribute__((visibility("default"))) int prism_moe_ep_forward(
   src.parity = &step->epoch;
   src.parity_stride_bytes = static_cast<int64_t>(back_stride);
   src.gate_err = err;
+  if (epilogue) {
+    src.residual = epilogue->residual;
+    src.norm_weight = epilogue->norm_weight;
+    src.residual_out = epilogue->residual_out;
+    src.eps = epilogue->eps;
+  }
   r = combine(land + LL.back, dtype, entry_row, w, T, k, hidden, out, st, &src);
   record_stage(6, st);
   return r;
+}
+
+__attribute__((visibility("default"))) int prism_moe_ep_forward(
+    const void* x, const void* router_logits, const int64_t* topk_ids_in,
+    const void* topk_weights_in, int dtype, int64_t num_tokens, int64_t max_tokens,
+    int64_t hidden, int64_t inter, int32_t num_experts, int32_t top_k, int32_t renorm,
+    int32_t ep_size, int32_t ep_rank, const void* w_gate_up, const void* w_down,
+    void* my_landing, const uint64_t* peer_landing, uint64_t epoch, void* out, void* workspace,
+    size_t workspace_bytes, void* stream) {
+  return prism_moe_ep_forward_norm(x, router_logits, topk_ids_in, topk_weights_in, dtype,
+                                   num_tokens, max_tokens, hidden, inter, num_experts, top_k,
+                                   renorm, ep_size, ep_rank, w_gate_up, w_down, my_landing,
+                                   peer_landing, epoch, out, workspace, workspace_bytes, stream,
+                                   nullptr);
 }
 
 __attribute__((visibility("default"))) int prism_moe_ep_read_stats(const void* workspace,

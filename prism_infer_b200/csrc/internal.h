@@ -119,12 +119,23 @@ int expert_swiglu_f32(const float* x, int64_t rows_cap, int64_t H, int64_t I,
 // combine.cu
 // With ``parity`` (EP steps): the rows are read from y + (*parity & 1) * parity_stride_bytes,
 // and a launch whose ``gate_err`` word holds PRISM_MOE_ERR_TIMEOUT writes nothing.
+// With ``norm_weight``: out = RMSNorm(residual + block output) and residual_out = the sum
+// (norm.cuh), the decoder layer's next add_rms_forward fused into the combine.
 struct CombineSource {
   const uint64_t* parity = nullptr;
   int64_t parity_stride_bytes = 0;
   const int* gate_err = nullptr;
+  const void* residual = nullptr;      // [T, H]
+  const void* norm_weight = nullptr;   // [H]
+  void* residual_out = nullptr;        // [T, H]
+  float eps = 1e-6f;
+  int64_t hidden = 0;                  // set by combine()
 };
 int combine(const void* y, int dtype, const int32_t* entry_row, const void* w, int64_t T, int k,
             int64_t hidden, void* out, cudaStream_t st, const CombineSource* src = nullptr);
+
+// norm.cu — RMSNorm (residual NULL) or residual add + RMSNorm of [T, H] rows.
+int rmsnorm(const void* x, const void* residual, const void* weight, float eps, int dtype,
+            int64_t T, int64_t hidden, void* out, void* residual_out, cudaStream_t st);
 
 }  // namespace prism

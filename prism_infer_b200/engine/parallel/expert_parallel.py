@@ -27,6 +27,8 @@ the grouped GEMM consumes directly. The per-expert row sequences are the referen
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
@@ -151,14 +153,18 @@ class ExpertParallelMoE(ExpertBank):
         self._p2p = None
 
     def forward_p2p(self, x: torch.Tensor, router_logits=None, topk_ids=None, topk_weights=None,
-                    top_k: int | None = None, renorm: bool = True) -> torch.Tensor:
+                    top_k: int | None = None, renorm: bool = True, residual=None,
+                    norm_weight=None, eps: float = 1e-6):
         """One step over NVLink peer memory: route (from logits, or given ids/weights), dispatch
         into the owners' landing zones, grouped experts, outputs stored back into the sources'
         landing zones by the down GEMM, combine. Collective over the EP group.
 
         The step's epoch is counted on the device (epoch argument 0), so after the first call
         (which reserves the landing zones, a collective that allocates) a step can be captured in
-        a CUDA graph and replayed; every rank must replay it the same number of times."""
+        a CUDA graph and replayed; every rank must replay it the same number of times.
+
+        With ``residual`` and ``norm_weight`` the final combine also applies the decoder layer's
+        next residual add + RMSNorm and the call returns (normalised, residual_out)."""
         T = x.shape[0]
         k = top_k if top_k is not None else topk_ids.shape[1]
         if self._p2p is None or self._p2p["top_k"] != k:
@@ -172,15 +178,18 @@ class ExpertParallelMoE(ExpertBank):
         ids = None if topk_ids is None else topk_ids.contiguous()
         w = None if topk_weights is None else topk_weights.to(x.dtype).contiguous()
         lg = None if router_logits is None else router_logits.contiguous()
+        res_out = torch.empty_like(x) if norm_weight is not None else None
+        epi = capi.norm_epilogue(None if residual is None else residual.contiguous(),
+                                 norm_weight, eps, res_out)
         lib = capi.load()
-        capi.check(lib.prism_moe_ep_forward(
+        capi.check(lib.prism_moe_ep_forward_norm(
             x.data_ptr(), capi.ptr(lg), capi.ptr(ids), capi.ptr(w), capi.BF16, T,
             st["max_tokens"], self.hidden_size, self.intermediate_size, self.num_experts, k,
             int(bool(renorm)), self.ep_size, self.ep_rank, self.w_gate_up.data_ptr(),
             self.w_down.data_ptr(), st["ptr"], st["table"].data_ptr(), 0,
-            out.data_ptr(), st["ws"].data_ptr(), st["ws"].numel(), capi.stream_of(x.device)),
-            "prism_moe_ep_forward")
-        return out
+            out.data_ptr(), st["ws"].data_ptr(), st["ws"].numel(), capi.stream_of(x.device),
+            None if epi is None else ctypes.byref(epi)), "prism_moe_ep_forward")
+        return out if epi is None else (out, res_out)
 
     def step_stats(self) -> dict:
         """Timing and row counts of the last step (``capi.ep_read_stats``; synchronises)."""

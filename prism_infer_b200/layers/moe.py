@@ -87,7 +87,16 @@ class MoE(ExpertBank):
         ids, w, _ = capi.route_topk(logits.contiguous(), self.top_k, self.norm_topk_prob)
         return logits, ids, w
 
-    def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
+    def forward(self, hidden_states: torch.Tensor, residual: torch.Tensor | None = None,
+                norm: nn.Module | None = None):
+        """``forward(hidden_states)`` -> the block output, as moe.py:69-100.
+
+        Decoder-layer fusion (optional): with ``residual`` (the layer's residual stream, shaped
+        like ``hidden_states``) and ``norm`` (the next layer's ``RMSNorm``: its ``weight`` and
+        ``eps`` are used), the combine kernel also applies ``norm(output, residual)`` and the call
+        returns ``(normalised, output + residual)`` — what prism_infer/models/qwen3.py:179-186
+        computes with the next layer's input_layernorm — without writing the block output.
+        """
         orig_shape = hidden_states.shape
         x = hidden_states.reshape(-1, orig_shape[-1])
         if not x.is_contiguous():
@@ -95,19 +104,35 @@ class MoE(ExpertBank):
         if x.dtype != self.gate.weight.dtype:
             raise RuntimeError(f"hidden_states dtype {x.dtype} != MoE weight dtype "
                                f"{self.gate.weight.dtype}")
+        fuse = norm is not None
+        if fuse and residual is None:
+            raise RuntimeError("MoE.forward: norm= needs residual=")
         logits = self.gate(x)                     # moe.py:74 — cuBLAS, as in the reference
+        renorm = bool(self.norm_topk_prob)
         if self.ep_size > 1:
             bank = self.ep_moe
             if bank.use_p2p(x):
+                if fuse:
+                    out, res = torch.ops.prism_moe.ep_forward_norm(
+                        x, logits, bank.w_gate_up, bank.w_down, self.top_k, renorm, bank.op_id,
+                        residual.reshape(x.shape), norm.weight, float(norm.eps))
+                    return out.view(orig_shape), res.view(orig_shape)
                 out = torch.ops.prism_moe.ep_forward(x, logits, bank.w_gate_up, bank.w_down,
-                                                     self.top_k, bool(self.norm_topk_prob),
-                                                     bank.op_id)
+                                                     self.top_k, renorm, bank.op_id)
                 return out.view(orig_shape)
-            ids, w = torch.ops.prism_moe.route_topk(logits, self.top_k,
-                                                    bool(self.norm_topk_prob))
-            return bank(x, ids, w).view(orig_shape)
+            ids, w = torch.ops.prism_moe.route_topk(logits, self.top_k, renorm)
+            out = bank(x, ids, w)
+            if fuse:
+                out, res = norm(out, residual.reshape(x.shape))
+                return out.view(orig_shape), res.view(orig_shape)
+            return out.view(orig_shape)
+        if fuse:
+            out, res = torch.ops.prism_moe.block_forward_norm(
+                x, logits, self.w_gate_up, self.w_down, self.top_k, renorm,
+                residual.reshape(x.shape), norm.weight, float(norm.eps))
+            return out.view(orig_shape), res.view(orig_shape)
         out = torch.ops.prism_moe.block_forward(x, logits, self.w_gate_up, self.w_down,
-                                                self.top_k, bool(self.norm_topk_prob))
+                                                self.top_k, renorm)
         return out.view(orig_shape)
 
     def check_device_error(self, device=None) -> None:

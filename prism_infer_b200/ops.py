@@ -23,6 +23,11 @@ Ops (shapes: T tokens, H hidden, E experts, k top-k, W expert-parallel ranks):
 * ``ep_forward(x, router_logits, w_gate_up[El,2I,H], w_down[El,H,I], top_k, renorm, bank)
   -> out[T,H]`` — moe.py:77-85 + expert_parallel.py:140-176 over NVLink peer memory; ``bank``
   names the ``ExpertParallelMoE`` whose landing zones the step uses (``ep_bank_id``).
+* ``rmsnorm(x[T,H], weight[H], eps) -> out`` and ``add_rmsnorm(x, residual, weight, eps) ->
+  (out, residual_out)`` — prism_infer/layers/layernorm.py:16-40.
+* ``block_forward_norm`` / ``ep_forward_norm``: the two block ops with the decoder layer's next
+  residual add + RMSNorm fused into the combine; extra arguments ``residual[T,H],
+  norm_weight[H], eps``; they return ``(out, residual_out)``.
 """
 from __future__ import annotations
 
@@ -140,3 +145,57 @@ def ep_forward(x: Tensor, router_logits: Tensor, w_gate_up: Tensor, w_down: Tens
 @ep_forward.register_fake
 def _(x, router_logits, w_gate_up, w_down, top_k, renorm, bank):
     return torch.empty_like(x)
+
+
+# ---------------------------------------------------------------------------------- norms
+
+@custom_op("prism_moe::rmsnorm", mutates_args=())
+def rmsnorm(x: Tensor, weight: Tensor, eps: float) -> Tensor:
+    return capi.rmsnorm(x, weight, eps)
+
+
+@rmsnorm.register_fake
+def _(x, weight, eps):
+    return torch.empty_like(x)
+
+
+@custom_op("prism_moe::add_rmsnorm", mutates_args=())
+def add_rmsnorm(x: Tensor, residual: Tensor, weight: Tensor, eps: float) -> tuple[Tensor, Tensor]:
+    return capi.rmsnorm(x, weight, eps, residual=residual)
+
+
+@add_rmsnorm.register_fake
+def _(x, residual, weight, eps):
+    return torch.empty_like(x), torch.empty_like(x)
+
+
+@custom_op("prism_moe::block_forward_norm", mutates_args=())
+def block_forward_norm(x: Tensor, router_logits: Tensor, w_gate_up: Tensor, w_down: Tensor,
+                       top_k: int, renorm: bool, residual: Tensor, norm_weight: Tensor,
+                       eps: float) -> tuple[Tensor, Tensor]:
+    residual = residual.contiguous()
+    res_out = torch.empty_like(x)
+    epi = capi.norm_epilogue(residual, norm_weight, eps, res_out)
+    out = capi.block_forward(x, router_logits, w_gate_up, w_down, top_k, renorm, epilogue=epi)
+    return out, res_out
+
+
+@block_forward_norm.register_fake
+def _(x, router_logits, w_gate_up, w_down, top_k, renorm, residual, norm_weight, eps):
+    return torch.empty_like(x), torch.empty_like(x)
+
+
+@custom_op("prism_moe::ep_forward_norm", mutates_args=())
+def ep_forward_norm(x: Tensor, router_logits: Tensor, w_gate_up: Tensor, w_down: Tensor,
+                    top_k: int, renorm: bool, bank: int, residual: Tensor, norm_weight: Tensor,
+                    eps: float) -> tuple[Tensor, Tensor]:
+    owner = _EP_BANKS.get(bank)
+    if owner is None:
+        raise RuntimeError("prism_moe::ep_forward_norm: unknown expert-parallel bank id")
+    return owner.forward_p2p(x, router_logits=router_logits, top_k=top_k, renorm=renorm,
+                             residual=residual, norm_weight=norm_weight, eps=eps)
+
+
+@ep_forward_norm.register_fake
+def _(x, router_logits, w_gate_up, w_down, top_k, renorm, bank, residual, norm_weight, eps):
+    return torch.empty_like(x), torch.empty_like(x)

@@ -2,7 +2,9 @@
 
 Usage (in a container where the reference source tree is available):
 
-    PRISM_REFERENCE=/path/to/prism-infer python tests/golden/make_golden.py
+    PRISM_REFERENCE=/path/to/prism-infer python tests/golden/make_golden.py [rmsnorm]
+
+(``rmsnorm`` writes only the RMSNorm fixtures.)
 
 Writes ``tests/golden/*.npz``. Inputs are regenerated from seeds by
 ``prism_infer_b200.synthetic`` (numpy PCG64, platform independent); the reference modules
@@ -207,10 +209,50 @@ def run_ep(case):
     return rec
 
 
+# (name, T, H, dtype, eps, seed): the decoder layer's RMSNorm (prism_infer/layers/layernorm.py),
+# run eagerly (its torch.compile is disabled here, as above)
+NORM_CASES = [
+    ("rmsnorm_fp32", 33, 256, "float32", 1e-6, 41),
+    ("rmsnorm_bf16", 8, 2048, "bfloat16", 1e-6, 42),
+    ("rmsnorm_bf16_eps", 5, 64, "bfloat16", 1e-2, 43),
+]
+
+
+def run_rmsnorm(name, T, H, dtype, eps, seed):
+    sys.path.insert(0, _ref_path())
+    import torch
+    from prism_infer.layers.layernorm import RMSNorm
+    tdt = torch.float32 if dtype == "float32" else torch.bfloat16
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal((T, H), dtype=np.float32) * 2).astype(np.float32)
+    res = rng.standard_normal((T, H), dtype=np.float32)
+    w = (1 + 0.25 * rng.standard_normal(H, dtype=np.float32)).astype(np.float32)
+    norm = RMSNorm(H, eps=eps)
+    with torch.no_grad():
+        norm.weight.copy_(torch.from_numpy(w))
+    norm = norm.to(tdt)
+    xt, rt = torch.from_numpy(x).to(tdt), torch.from_numpy(res).to(tdt)
+    with torch.no_grad():
+        rms = norm(xt.clone())
+        add, add_res = norm(xt.clone(), rt.clone())
+    f = lambda t: t.detach().float().numpy()
+    return dict(x=f(xt), residual=f(rt), weight=f(norm.weight), eps=np.float32(eps),
+                dtype=dtype, rms_out=f(rms), add_out=f(add), add_residual=f(add_res))
+
+
 def main():
+    only = sys.argv[1:]
+    if only == ["rmsnorm"]:
+        for case in NORM_CASES:
+            np.savez_compressed(HERE / f"{case[0]}.npz", **run_rmsnorm(*case))
+            print("wrote", case[0])
+        return
     MoE, _ = _import_reference()
     import torch
     torch.manual_seed(0)
+    for case in NORM_CASES:
+        np.savez_compressed(HERE / f"{case[0]}.npz", **run_rmsnorm(*case))
+        print("wrote", case[0])
     for case in SINGLE_CASES:
         rec = run_single(MoE, *case)
         np.savez_compressed(HERE / f"{case[0]}.npz", **rec)

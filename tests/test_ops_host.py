@@ -8,7 +8,8 @@ from torch._subclasses.fake_tensor import FakeTensorMode
 from prism_infer_b200 import ops  # noqa: F401  (registers the ops)
 
 OPS = ("route_topk", "dispatch_plan", "permute_rows", "combine", "expert_swiglu",
-       "block_forward", "ep_forward")
+       "block_forward", "ep_forward", "rmsnorm", "add_rmsnorm", "block_forward_norm",
+       "ep_forward_norm")
 
 
 def test_ops_are_registered():
@@ -41,6 +42,12 @@ def test_fake_shapes():
         assert out.shape == (T, H) and out.dtype == x.dtype
         blk = torch.ops.prism_moe.block_forward(x, logits, wgu, wd, k, True)
         assert blk.shape == x.shape and blk.dtype == x.dtype
+        nw = torch.empty(H, device=dev, dtype=torch.bfloat16)
+        assert torch.ops.prism_moe.rmsnorm(x, nw, 1e-6).shape == x.shape
+        o, r = torch.ops.prism_moe.add_rmsnorm(x, x, nw, 1e-6)
+        assert o.shape == r.shape == x.shape
+        o, r = torch.ops.prism_moe.block_forward_norm(x, logits, wgu, wd, k, True, x, nw, 1e-6)
+        assert o.shape == r.shape == x.shape and o.dtype == x.dtype
 
 
 def test_moe_exports_as_one_graph():
@@ -64,3 +71,35 @@ def test_cpu_tensors_raise():
     x = torch.zeros(4, 8, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="CUDA"):
         torch.ops.prism_moe.route_topk(x, 2, True)
+
+
+def test_decoder_layer_fusion_exports_as_one_graph():
+    """post_attention_layernorm (the drop-in RMSNorm) -> MoE with the next layer's
+    input_layernorm fused into its combine, exported on meta tensors."""
+    from torch import nn
+
+    from prism_infer_b200.engine.parallel import set_expert_parallel_size
+    from prism_infer_b200.layers.layernorm import RMSNorm
+    from prism_infer_b200.layers.moe import MoE
+    set_expert_parallel_size(1)
+    H, E, k, I = 64, 16, 4, 32
+
+    class Tail(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.post_attention_layernorm = RMSNorm(H)
+            self.mlp = MoE(H, I, E, k)
+            self.next_input_layernorm = RMSNorm(H)
+
+        def forward(self, hidden, residual):
+            hidden, residual = self.post_attention_layernorm(hidden, residual)
+            return self.mlp(hidden, residual=residual, norm=self.next_input_layernorm)
+
+    tail = Tail().to("meta", torch.bfloat16)
+    x = torch.empty(7, H, device="meta", dtype=torch.bfloat16)
+    out, res = tail(x, x)
+    assert out.shape == res.shape == x.shape
+    ep = torch.export.export(tail, (x, x))
+    called = [str(n.target) for n in ep.graph.nodes if n.op == "call_function"]
+    assert "prism_moe.add_rmsnorm.default" in called
+    assert "prism_moe.block_forward_norm.default" in called
