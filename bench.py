@@ -73,6 +73,7 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-extra-configs", action="store_true")
+    ap.add_argument("--no-ep1", action="store_true")
     return ap.parse_args()
 
 
@@ -367,6 +368,45 @@ def a2a_stats(moe, x, world, reps=5):
     }
 
 
+def ep_path_one_gpu(moe, x, device, peak, steps=20, warmup=3):
+    """The expert-parallel step (``prism_moe_ep_forward``) at ep_size 1 on the block's weights:
+    the same kernels as at EP>1 (counts exchange, fused expert launch with its copy warps,
+    return wait, combine), against this GPU's own landing zone. Shows what the exchange
+    machinery costs without NVLink, and is the launch an ncu capture on one GPU sees."""
+    import torch
+
+    from prism_infer_b200.engine.parallel.expert_parallel import ExpertParallelMoE
+    c = CFGS[2]
+    bank = ExpertParallelMoE(c["H"], c["I"], c["E"], 1, 0, transport="p2p").to(device,
+                                                                               torch.bfloat16)
+    with torch.no_grad():
+        bank.w_gate_up.copy_(moe.w_gate_up)
+        bank.w_down.copy_(moe.w_down)
+    holder = {}
+
+    def step(_i):
+        with torch.inference_mode():
+            holder["y"] = bank.forward_p2p(x, router_logits=moe.gate(x), top_k=c["k"])
+    ms = time_device(step, steps, warmup, 1)
+    st = bank.step_stats()
+    bank.check_device_error()
+    with torch.inference_mode():
+        same = bool(torch.equal(holder["y"], moe(x)))
+    fused_ms = (st["fused_t1_ns"] - st["fused_t0_ns"]) / 1e6
+    T = x.shape[0]
+    kflops = 2.0 * T * c["k"] * c["H"] * 3 * c["I"]
+    res = {"ms_per_step": ms / steps, "tokens_per_s": T / (ms / steps / 1e3),
+           "fused_launch_ms": fused_ms,
+           "fused_launch_tflops": kflops / (fused_ms / 1e3) / 1e12 if fused_ms > 0 else None,
+           "fused_launch_frac_of_peak": (kflops / (fused_ms / 1e3) / 1e12 / peak
+                                         if fused_ms > 0 else None),
+           "output_equals_block_path": same,
+           "how": "ExpertParallelMoE(ep_size=1).forward_p2p; fused launch span from its "
+                  "%globaltimer stamps (last step)"}
+    bank.release()
+    return res
+
+
 def sub_config(cfg_id, world, rank, device, peak, steps=10, warmup=3):
     """Throughput and parity of benchmark config ``cfg_id`` at EP=world."""
     c = CFGS[cfg_id]
@@ -642,6 +682,9 @@ def run_ours(args):
         extra["decode_cfg1"]["graph_ms_per_step"] = ms_g / 200
         extra["decode_cfg1"]["graph_hbm_gbs"] = wbytes / (ms_g / 200 / 1e3) / 1e9
         del graph
+
+    if world == 1 and not args.no_ep1:
+        extra["ep_path_1gpu"] = ep_path_one_gpu(moe, x, device, peak)
 
     free_block(moe, world)
     del x_dev, y_dev

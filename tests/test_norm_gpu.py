@@ -3,7 +3,7 @@ around the MoE block, prism_infer/models/qwen3.py:179-186):
 
 * ``prism_moe_rmsnorm`` (the drop-in ``RMSNorm``) against the reference's own module outputs
   (golden fixtures) and against the oracle at the block's shapes: the residual sum bit for bit,
-  the normalised rows within one bf16 unit in the last place (the reference's sum of squares is
+  the normalised rows within two bf16 units in the last place (the reference's sum of squares is
   Inductor's, in another order) and the fp32 suite tolerance;
 * the block with the next layer's residual add + RMSNorm fused into its combine: bit for bit the
   unfused sequence (block, then ``prism_moe_rmsnorm``), for the single-GPU block and for the
@@ -42,8 +42,11 @@ def check_norm(got, ref, dtype):
     if dtype == torch.float32:
         np.testing.assert_allclose(got, ref, atol=1e-5, rtol=1e-4)
     else:
+        # the sum of squares runs in another order (and rsqrt may differ in its last bit): a
+        # normalised value near a rounding boundary can land one bf16 step away, and the
+        # product with the weight can widen that to two
         u = _ulps_bf16(got, ref)
-        assert u.max() <= 1 and (u > 0).mean() < 0.01, (u.max(), (u > 0).mean())
+        assert u.max() <= 2 and (u > 0).mean() < 0.01, (u.max(), (u > 0).mean())
 
 
 @pytest.mark.parametrize("name", ["rmsnorm_fp32", "rmsnorm_bf16", "rmsnorm_bf16_eps"])
