@@ -109,6 +109,53 @@ __device__ __forceinline__ uint32_t load_acquire_sys(const uint32_t* p) {
 __device__ __forceinline__ void add_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// The same within one GPU (the writer and every reader on this GPU).
+__device__ __forceinline__ void add_release_gpu_u32(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Spin-wait building blocks: poll with relaxed loads, then one acquire fence once the value is
+// seen (a relaxed read followed by fence.acq_rel is an acquire pattern), instead of an acquire
+// load, which carries a fence, on every iteration.
+__device__ __forceinline__ uint64_t load_relaxed_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t load_relaxed_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+__device__ __forceinline__ void store_release_gpu(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Fences and flag stores at the narrowest scope that covers every GPU involved: system scope
+// only when another GPU reads or wrote the data. (A system-scope fence also waits for this GPU's
+// traffic to the host, e.g. copies that a serving loop overlaps with the step.)
+__device__ __forceinline__ void threadfence_scoped(bool sys) {
+  if (sys)
+    __threadfence_system();
+  else
+    __threadfence();
+}
+__device__ __forceinline__ void fence_acq_rel_scoped(bool sys) {
+  if (sys)
+    fence_acq_rel_sys();
+  else
+    fence_acq_rel_gpu();
+}
+__device__ __forceinline__ void store_release_scoped(uint64_t* p, uint64_t v, bool sys) {
+  if (sys)
+    store_release_sys(p, v);
+  else
+    store_release_gpu(p, v);
+}
 
 // Device error word: the first failing kernel records its code; the host reads it.
 __device__ __forceinline__ void record_device_error(int* err, int code) {

@@ -7,8 +7,9 @@
 // identical offsets on every rank:
 //   flags   [2 phases][W] u64   phase A counts ready, C outputs landed; slot s is written
 //                               (st.release.sys) by source rank s with the step's epoch
-//   arrive  [2][W*El] u32       per-parity rows landed in each receive segment (red.release.sys
-//                               by the senders' copy warps; reset one step ahead by the owner)
+//   arrive  [2][El+W] u32       per-parity arrival counters: rows landed in each own-expert
+//                               segment (El) and from each other source (W); release adds by
+//                               the senders' copy warps, reset one step ahead by the owner
 //   counts  [2][W][E] i32       per-parity all-gathered expert histograms (row = source rank)
 //   recv    [2][W*Tmax*k][H]    rows routed to this rank's experts, in W*El segments ordered by
 //                               expected arrival (ep_counts_kernel)
@@ -43,8 +44,9 @@ namespace {
 
 constexpr int kMaxRanks = 64;
 constexpr int kMaxExperts = 1024;
-// flags (2 x 64 x 8 B, padded to 4 KB) + arrival counters (2 x 1024 x 4 B); zero at allocation
-constexpr size_t kHeaderBytes = 4096 + 2 * kMaxExperts * sizeof(uint32_t);
+// flags (2 x 64 x 8 B, padded to 4 KB) + arrival counters (2 x (1024 + 64) x 4 B); zero at
+// allocation
+constexpr size_t kHeaderBytes = 4096 + 2 * (kMaxExperts + kMaxRanks) * sizeof(uint32_t);
 constexpr size_t kCountsMaxBytes = sizeof(int32_t) * 2 * kMaxRanks * kMaxExperts;
 
 struct Landing {
@@ -73,7 +75,7 @@ Landing landing_layout(int W, int64_t max_tokens, int k, int64_t H, int E, int64
 
 struct EpWs {
   size_t err, ids, w, plan, plan_bytes, counts, offsets, entry_row, row_entry, seg_offsets,
-      seg_expert, seg_base, dst_base, flag_c, done, h, total;
+      seg_expert, seg_base, dst_base, src_rows, flag_c, done, h, total;
 };
 
 EpWs ep_ws_layout(int64_t max_tokens, int64_t H, int64_t I, int E, int k, int W, int64_t rcap,
@@ -99,6 +101,7 @@ EpWs ep_ws_layout(int64_t max_tokens, int64_t H, int64_t I, int E, int k, int W,
   L.seg_expert = take(sizeof(int32_t) * E);
   L.seg_base = take(sizeof(uint64_t) * E);
   L.dst_base = take(sizeof(int32_t) * E);
+  L.src_rows = take(sizeof(int32_t) * W);
   L.flag_c = take(sizeof(uint64_t) * W);
   L.done = take(sizeof(unsigned int) * 4);   // chunk claim, chunks stored, CTAs done
   L.h = take(expert_scratch_bytes(rcap, I, es));
@@ -117,13 +120,14 @@ __device__ bool wait_flags(const uint64_t* local_flags, int W, uint64_t epoch, i
   bool ok = true;
   if (s < W) {
     const uint64_t t0 = global_timer_ns();
-    while (load_acquire_sys(local_flags + s) != epoch) {
+    while (load_relaxed_sys(local_flags + s) != epoch) {
       if (global_timer_ns() - t0 > limit_ns) {
         record_device_error(err, PRISM_MOE_ERR_TIMEOUT);
         ok = false;
         break;
       }
     }
+    fence_acq_rel_scoped(W > 1);   // with the relaxed poll above: acquire of the flag stores
   }
   return ok;
 }
@@ -166,6 +170,7 @@ struct CountsArgs {
   int32_t* seg_expert;        // [W*El]
   uint64_t* seg_base;         // [W*El]
   int32_t* dst_base;          // [E]
+  int32_t* src_rows;          // [W] rows received in slot j, from source (me - j) mod W
   uint64_t* flag_c;           // [W]
   unsigned int* claim;        // [0] chunk claim, [1] chunks stored
   int* err;
@@ -210,9 +215,10 @@ __global__ void __launch_bounds__(1024) ep_counts_kernel(const CountsArgs a) {
     int32_t* dst = reinterpret_cast<int32_t*>(peers[d] + counts_off) + (par * W + me) * E;
     dst[e] = my_counts[e];
   }
-  __threadfence_system();
+  threadfence_scoped(W > 1);
   __syncthreads();
-  if (threadIdx.x < W) store_release_sys(flag_addr(peers[threadIdx.x], flags_off, W, 0, me), epoch);
+  if (threadIdx.x < W)
+    store_release_scoped(flag_addr(peers[threadIdx.x], flags_off, W, 0, me), epoch, W > 1);
   // 2. wait for every source's histogram
   const uint64_t* my_flags = flag_addr(peers[me], flags_off, W, 0, 0);
   wait_flags(my_flags, W, epoch, err, a.peer_wait_ns);
@@ -251,6 +257,7 @@ __global__ void __launch_bounds__(1024) ep_counts_kernel(const CountsArgs a) {
     a.step->send_rows = send;
     a.step->recv_rows = recv;
   }
+  if (i < W) a.src_rows[i] = R[me * W + (me - i + W) % W];
   // 5. where my rows of expert e start in its owner's receive layout
   const int32_t mine = i < E ? C[me * E + i] : 0;
   const int32_t my_ex = block_excl_scan(mine, E, tmp, nullptr);
@@ -296,8 +303,8 @@ __global__ void __launch_bounds__(1024) ep_counts_kernel(const CountsArgs a) {
   uint32_t* next_arrive = reinterpret_cast<uint32_t*>(
       peers[me] + a.arrive_off + static_cast<size_t>(par ^ 1) * a.arrive_stride);
   if (i < 2) a.claim[i] = 0u;
-  if (i < E) next_arrive[i] = 0u;
-  __threadfence_system();
+  for (int c = i; c < El + W; c += blockDim.x) next_arrive[c] = 0u;
+  threadfence_scoped(W > 1);
   if (i < W) a.flag_c[i] = reinterpret_cast<uint64_t>(flag_addr(peers[i], flags_off, W, 1, me));
 }
 
@@ -313,7 +320,7 @@ __global__ void ep_wait_kernel(const uint64_t* __restrict__ peers, int me, size_
   if (s_skip) return;
   wait_flags(flag_addr(peers[me], flags_off, W, phase, 0), W, step->epoch, err, limit_ns);
   __syncthreads();
-  __threadfence_system();
+  threadfence_scoped(W > 1);
 }
 
 }  // namespace
@@ -455,7 +462,7 @@ __attribute__((visibility("default"))) int prism_moe_ep_forward_norm(
   char* land = static_cast<char*>(my_landing);
   const size_t recv_stride = static_cast<size_t>(LL.rcap) * hidden * es;
   const size_t back_stride = static_cast<size_t>(LL.bcap) * hidden * es;
-  const size_t arrive_stride = static_cast<size_t>(E) * sizeof(uint32_t);
+  const size_t arrive_stride = static_cast<size_t>(El + W) * sizeof(uint32_t);
 
   CountsArgs ca{};
   ca.my_counts = counts;
@@ -476,6 +483,7 @@ __attribute__((visibility("default"))) int prism_moe_ep_forward_norm(
   ca.seg_expert = seg_expert;
   ca.seg_base = seg_base;
   ca.dst_base = dst_base;
+  ca.src_rows = reinterpret_cast<int32_t*>(ws + L.src_rows);
   ca.flag_c = flag_c;
   ca.claim = done;
   ca.err = err;
@@ -495,6 +503,7 @@ __attribute__((visibility("default"))) int prism_moe_ep_forward_norm(
   disp.row_entry = row_entry;
   disp.expert_offsets = offsets;
   disp.dst_base = dst_base;
+  disp.src_rows = reinterpret_cast<int32_t*>(ws + L.src_rows);
   disp.peers = peer_landing;
   for (int p = 0; p < 2; ++p) {
     disp.recv_off[p] = LL.recv + p * recv_stride;
@@ -515,6 +524,7 @@ __attribute__((visibility("default"))) int prism_moe_ep_forward_norm(
   down.epoch_ptr = &step->epoch;
   down.done_counter = done + 2;
   down.step = step;
+  down.remote = W > 1;
   r = expert_swiglu_bf16(land + LL.recv, LL.rcap, hidden, inter, seg_offsets, seg_expert, E, El,
                          w_gate_up, w_down, nullptr, ws + L.h, err, st, &down, &disp);
   if (r) return r;

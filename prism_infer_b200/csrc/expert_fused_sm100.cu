@@ -14,7 +14,7 @@
 // claim, so the launch makes progress even when the GPU holds fewer CTAs than the grid.
 //
 // With expert parallelism (``GemmDispatch``) four more warps per CTA dispatch this rank's
-// expert-major rows into the owners' receive buffers inside the same launch: 16-row chunks
+// expert-major rows into the owners' receive buffers inside the same launch: 32-row chunks
 // claimed from a shared counter, peers in rotated order, each run of one expert's rows
 // published on the owner's per-segment arrival counter (release, system scope); the producer
 // of a gate_up tile waits for its segment's counter. The down epilogue stores every output row
@@ -109,17 +109,37 @@ __device__ __forceinline__ void add_release_gpu(unsigned int* p, uint32_t v) {
 // ---------------------------------------------------------------------------------------------
 // copy warps (expert parallelism)
 // ---------------------------------------------------------------------------------------------
-// Dispatch: ``n`` rows of expert ``e`` are written; publish them to the owner's arrival counter
-// of the receive segment they belong to.
-__device__ __forceinline__ void dispatch_flush(const GemmDispatch& D, size_t arrive_off,
-                                               int64_t e, unsigned int n, int lane) {
-  __threadfence_system();
+// Rows per dispatch chunk (one lane looks up each row): the unit copy warps claim, and at most
+// one publish per arrival counter inside it.
+constexpr int kChunkRows = 32;
+
+// Arrival counter (on the owner) that a row for expert ``e`` counts on. The owner's receive slot
+// j = (d - me) mod W holds this rank's rows; slot 0 (this rank's own experts, copied first) has
+// one counter per local expert so the GEMM can start on the first segments, counters 0..El-1;
+// every other slot has one counter for the whole slot, counter El + j, so that an owner does
+// one system-scope acquire per source and CTA rather than one per segment.
+__device__ __forceinline__ int arrival_counter(const GemmDispatch& D, int64_t e, int d) {
+  return d == D.me ? static_cast<int>(e - static_cast<int64_t>(d) * D.El)
+                   : D.El + (d - D.me + D.W) % D.W;
+}
+
+// Dispatch: ``n`` rows for owner ``d`` are written; publish them on the owner's arrival counter
+// ``ctr``. The warp barrier orders every lane's stores before lane 0's release add
+// (cumulative). Rows for this rank's own experts are published at GPU scope: a system-scope
+// release also waits for this GPU's traffic to the host (copies running beside the step), which
+// an owner on the same GPU does not need.
+__device__ __forceinline__ void dispatch_flush(const GemmDispatch& D, size_t arrive_off, int ctr,
+                                               unsigned int n, int lane) {
   __syncwarp();
   if (lane == 0) {
-    const int d = static_cast<int>(e / D.El);
-    const int j = (d - D.me + D.W) % D.W;
-    const int sg = j * D.El + static_cast<int>(e - static_cast<int64_t>(d) * D.El);
-    add_release_sys(reinterpret_cast<uint32_t*>(D.peers[d] + arrive_off) + sg, n);
+    const int d = ctr < D.El ? D.me : (D.me + ctr - D.El) % D.W;
+    uint32_t* counter = reinterpret_cast<uint32_t*>(D.peers[d] + arrive_off) + ctr;
+    if (d == D.me) {
+      add_release_gpu_u32(counter, n);
+    } else {
+      __threadfence_system();
+      add_release_sys(counter, n);
+    }
   }
   __syncwarp();
 }
@@ -145,29 +165,30 @@ __device__ __forceinline__ void copy_row_pair(const uint4* sa, uint4* da, const 
   }
 }
 
-// One 16-row dispatch chunk of this rank's expert-major rows [0, n), own block first and then
+// One dispatch chunk (kChunkRows rows) of this rank's expert-major rows [0, n), own block first and then
 // the following ranks' blocks. Lanes look up the chunk's rows at once; rows then move in pairs.
 // Every row below n belongs to an entry with a valid expert id (the plan leaves the others out),
 // so every store lands inside an owner's receive buffer.
 __device__ void dispatch_chunk(const GemmDispatch& D, int64_t c, int64_t n, int par, int lane) {
-  constexpr int kChunkRows = 16;
   const int64_t shift = D.expert_offsets[D.me * D.El];
   const int64_t i0 = c * kChunkRows;
   const int nr = static_cast<int>(n - i0 < kChunkRows ? n - i0 : kChunkRows);
   const uint4* x = static_cast<const uint4*>(D.x);
   const size_t recv_off = D.recv_off[par], arrive_off = D.arrive_off[par];
-  int64_t my_e = -1, my_src = 0;
+  int my_ctr = -1;
+  int64_t my_src = 0;
   uint64_t my_dst = 0;
   if (lane < nr) {
     const int64_t q = (i0 + lane + shift) % n;
     const int32_t f = D.row_entry[q];
-    my_e = D.ids[f];
+    const int64_t e = D.ids[f];
     my_src = f / D.k;
-    const int d = static_cast<int>(my_e / D.El);
-    const int64_t dst_row = D.dst_base[my_e] + (q - D.expert_offsets[my_e]);
+    const int d = static_cast<int>(e / D.El);
+    my_ctr = arrival_counter(D, e, d);
+    const int64_t dst_row = D.dst_base[e] + (q - D.expert_offsets[e]);
     my_dst = D.peers[d] + recv_off + static_cast<uint64_t>(dst_row * D.vpr * 16);
   }
-  int64_t e_run = -1;
+  int c_run = -1;
   unsigned int n_run = 0;
   for (int r = 0; r < nr; r += 2) {
     const bool two = r + 1 < nr;
@@ -177,25 +198,24 @@ __device__ void dispatch_chunk(const GemmDispatch& D, int64_t c, int64_t n, int 
                   x + __shfl_sync(0xffffffffu, my_src, rb) * D.vpr,
                   reinterpret_cast<uint4*>(__shfl_sync(0xffffffffu, my_dst, rb)), two, D.vpr,
                   lane);
-    // runs of one expert; a run's rows are all stored before its count is published
+    // runs of one arrival counter; a run's rows are all stored before its count is published
     for (int t = r; t <= rb; ++t) {
-      const int64_t e = __shfl_sync(0xffffffffu, my_e, t);
-      if (e != e_run) {
-        if (n_run) dispatch_flush(D, arrive_off, e_run, n_run, lane);
-        e_run = e;
+      const int ctr = __shfl_sync(0xffffffffu, my_ctr, t);
+      if (ctr != c_run) {
+        if (n_run) dispatch_flush(D, arrive_off, c_run, n_run, lane);
+        c_run = ctr;
         n_run = 0;
       }
       ++n_run;
     }
   }
-  if (n_run) dispatch_flush(D, arrive_off, e_run, n_run, lane);
+  if (n_run) dispatch_flush(D, arrive_off, c_run, n_run, lane);
 }
 
-// Copy-warp loop: claim 16-row dispatch chunks until none are left. The rows to send are the
+// Copy-warp loop: claim dispatch chunks until none are left. The rows to send are the
 // plan's valid rows, expert_offsets[E] of them. The warp that claims the first chunk and the
 // warp that stores the last one stamp the step's dispatch window.
 __device__ void copy_warp_loop(const GemmDispatch& D, int par, int lane) {
-  constexpr int kChunkRows = 16;
   const int64_t n = D.expert_offsets[D.E];
   const int64_t nchunks = (n + kChunkRows - 1) / kChunkRows;
   for (;;) {
@@ -299,7 +319,7 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
     uint32_t issued = 0, issued_parity = 0;
     int rslot = 0;
     uint32_t rphase = 0;
-    int ready_seg = -1;      // dispatch: every row of this segment has landed
+    int ready_key = -1;      // dispatch: the last arrival counter seen complete
     int32_t ready_mt = -1;   // every h row of this m-tile is stored
     bool ok = true;
     const uint32_t* my_arrive =
@@ -328,17 +348,26 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
       const int32_t row0 = P.seg_offsets[s] + (tr.mt - prefix[s]) * 128;
       const uint64_t t0 = global_timer_ns();
       if (tr.kind == 0) {
-        if (kDispatch && s != ready_seg) {
-          const uint32_t need = static_cast<uint32_t>(P.seg_offsets[s + 1] - P.seg_offsets[s]);
-          while (load_acquire_sys(my_arrive + s) != need) {
+        // receive slot j of segment s (rows from source (me - j) mod W) and its counter: one per
+        // segment in slot 0, one per slot after it. Counters only grow along the tile stream,
+        // and this CTA claims stream positions in increasing order.
+        const int j = kDispatch ? s / disp.El : 0;
+        const int key = j == 0 ? s : disp.El + j;
+        if (kDispatch && key > ready_key) {
+          const uint32_t need =
+              static_cast<uint32_t>(j == 0 ? P.seg_offsets[s + 1] - P.seg_offsets[s]
+                                           : disp.src_rows[j]);
+          while (load_relaxed_sys(my_arrive + key) != need) {
             if (*abort || global_timer_ns() - t0 > P.peer_wait_ns) {
               ok = false;
               break;
             }
           }
+          // acquire: the source's rows before the counter it raised (slot 0 is this GPU itself)
+          fence_acq_rel_scoped(j > 0);
           // rows written through the generic proxy (peer stores), read next by TMA
           asm volatile("fence.proxy.async.global;" ::: "memory");
-          ready_seg = s;
+          ready_key = key;
         }
       } else if (tr.mt != ready_mt) {
         while (load_acquire_gpu(P.h_ready + tr.mt) != h_target) {
@@ -507,7 +536,7 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
     }
   }
 
-  if (tgt.done_counter != nullptr && warp >= 2) __threadfence_system();
+  if (tgt.done_counter != nullptr && warp >= 2) threadfence_scoped(tgt.remote);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -517,14 +546,15 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
   }
   // completion signal: the last CTA to get here publishes `epoch` to every flag
   if (tgt.done_counter != nullptr && threadIdx.x == 0) {
-    __threadfence_system();
+    threadfence_scoped(tgt.remote);
     const unsigned int prev = atomicAdd(tgt.done_counter, 1u);
     if (prev == gridDim.x - 1) {
       *tgt.done_counter = 0u;  // ready for the next launch (stream-ordered)
       if (tgt.step) tgt.step->fused_t1 = global_timer_ns();
-      __threadfence_system();
+      threadfence_scoped(tgt.remote);
       const uint64_t ep = tgt.epoch_ptr ? *tgt.epoch_ptr : tgt.epoch;
-      for (int i = 0; i < tgt.num_signal; ++i) store_release_sys(tgt.signal_flags[i], ep);
+      for (int i = 0; i < tgt.num_signal; ++i)
+        store_release_scoped(tgt.signal_flags[i], ep, tgt.remote);
     }
   }
 }

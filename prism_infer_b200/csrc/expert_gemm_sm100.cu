@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  if (tgt.done_counter != nullptr && warp >= 2) __threadfence_system();
+  if (tgt.done_counter != nullptr && warp >= 2) threadfence_scoped(tgt.remote);
   tc_fence_before();
   if constexpr (kPair)
     cluster_sync();   // neither CTA leaves while its partner may still use its TMEM / smem
@@ -277,13 +277,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   // completion signal: the last CTA to get here publishes `epoch` to every flag
   if (tgt.done_counter != nullptr && threadIdx.x == 0) {
-    __threadfence_system();
+    threadfence_scoped(tgt.remote);
     const unsigned int prev = atomicAdd(tgt.done_counter, 1u);
     if (prev == gridDim.x - 1) {
       *tgt.done_counter = 0u;  // ready for the next launch (stream-ordered)
-      __threadfence_system();
+      threadfence_scoped(tgt.remote);
       const uint64_t ep = tgt.epoch_ptr ? *tgt.epoch_ptr : tgt.epoch;
-      for (int i = 0; i < tgt.num_signal; ++i) store_release_sys(tgt.signal_flags[i], ep);
+      for (int i = 0; i < tgt.num_signal; ++i)
+        store_release_scoped(tgt.signal_flags[i], ep, tgt.remote);
     }
   }
 }

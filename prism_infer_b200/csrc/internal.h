@@ -36,15 +36,18 @@ struct GemmOutput {
   const uint64_t* epoch_ptr = nullptr;
   unsigned int* done_counter = nullptr;
   EpStepState* step = nullptr;   // launch timing (fused_t0 / fused_t1), or NULL
+  bool remote = false;           // rows or flags may live on other GPUs: system-scope fences
 };
 
 // Expert-parallel exchange carried out INSIDE the fused expert launch (ep.cu): extra copy warps
 // write this rank's expert-major rows into the owners' receive buffers, peers in rotated order
-// starting with this rank itself, and after each run of rows of one expert add the run's length
-// to that receive segment's arrival counter on the owner. The receive layout on rank d is
-// segment (j, le), index j * El + le = rows of local expert le from source (d - j) mod W. The
-// GEMM's producer waits (bounded) until the arrival counter of the segment a tile reads equals
-// the segment's row count. Every per-parity field is indexed by ``*epoch_ptr & 1``.
+// starting with this rank itself, and after each run of rows for one arrival counter add the
+// run's length to it on the owner. The receive layout on rank d is segment (j, le), index
+// j * El + le = rows of local expert le from source (d - j) mod W. Arrival counters: one per
+// segment of slot 0 (the owner's own rows, counters 0..El-1) and one per later slot (counter
+// El + j, all rows from that source). The GEMM's producer waits (bounded) until the counter of
+// the segment a tile reads equals its row count (slot 0) or src_rows[j]. Every per-parity field
+// is indexed by ``*epoch_ptr & 1``.
 // Only rows [0, expert_offsets[E]) are sent: entries with an expert id outside [0, E) have no
 // row (the dispatch plan leaves them out) and are never copied anywhere.
 struct GemmDispatch {
@@ -56,12 +59,13 @@ struct GemmDispatch {
   const int32_t* row_entry = nullptr;   // [T*k] expert-major row -> flat entry
   const int32_t* expert_offsets = nullptr;   // [E+1]
   const int32_t* dst_base = nullptr;    // [E] first row of my expert-e rows in the owner's layout
+  const int32_t* src_rows = nullptr;    // [W] rows this rank receives in slot j (all its segments)
   const uint64_t* peers = nullptr;      // [W] landing-zone base addresses
   const void* x_recv[2] = {nullptr, nullptr};   // this rank's receive buffers (GEMM A operand)
   size_t recv_off[2] = {0, 0};          // byte offsets of the receive buffers in a landing zone
   size_t arrive_off[2] = {0, 0};        // byte offsets of the [W*El] u32 arrival counters
   const uint64_t* epoch_ptr = nullptr;  // the step's epoch (EpStepState::epoch)
-  unsigned int* claim = nullptr;        // [0] next 16-row chunk to copy, [1] chunks stored
+  unsigned int* claim = nullptr;        // [0] next dispatch chunk to copy, [1] chunks stored
   EpStepState* step = nullptr;          // dispatch timing, or NULL
   const int* gate_err = nullptr;        // the launch does nothing when this holds ERR_TIMEOUT
   int W = 1, me = 0, El = 1;
