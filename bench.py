@@ -354,17 +354,20 @@ def a2a_stats(moe, x, world, reps=5):
     acc = [a / reps for a in acc]
     tot = reduce_over_ranks(acc, "sum", world)
     mean = [t / world for t in tot]
+    T, k = x.shape[0], CFGS[2]["k"]
     return {
         "dispatch_remote_bytes_per_rank": mean[0],
         "return_remote_bytes_per_rank": mean[1],
+        "dispatch_bytes_without_dedup_per_rank": T * k * (world - 1) / world * H * 2,
         "dispatch_ms": mean[2] / 1e6,
         "fused_launch_ms": mean[3] / 1e6,
         "dispatch_gbs": mean[0] / mean[2],
-        "nvlink_out_gbs_over_fused_launch": mean[4],
+        "nvlink_gbs_over_fused_launch": mean[4],
         "landing_zone_bytes_per_rank": moe.ep_moe.landing_bytes(),
-        "how": "per rank: rows sent to / returned to other ranks x H x 2 B; dispatch window = "
-               "first chunk claimed to last chunk stored (%globaltimer in the copy warps); "
-               "mean over ranks and 5 steps",
+        "how": "per rank: token rows pulled from other ranks (one per token and rank) and rows "
+               "returned to them (one per routed entry) x H x 2 B; the no-dedup figure assumes "
+               "uniform routing; dispatch window = first chunk claimed to last chunk stored "
+               "(%globaltimer in the copy warps); mean over ranks and steps",
     }
 
 

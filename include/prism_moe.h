@@ -279,9 +279,10 @@ size_t prism_moe_ep_workspace_size(int64_t max_tokens, int64_t hidden, int64_t i
  *   my_landing: this rank's landing zone; peer_landing: DEVICE array of W uint64 landing-zone
  *   addresses as mapped in this process (entry ep_rank = my_landing).
  * T <= max_tokens (the landing capacity). Kernels: route (when logits are given), dispatch plan,
- * counts all-gather, one fused expert launch (both GEMMs; its copy warps write the rows into the
- * owners' receive buffers, its down epilogue writes the outputs back into the sources' buffers),
- * wait for the returned rows, combine.
+ * a copy of x into the landing zone, counts all-gather, one fused expert launch (both GEMMs; its
+ * copy warps fill this rank's receive buffer, pulling the rows other ranks routed here over
+ * NVLink, one row per token and rank; its down epilogue writes the outputs back into the
+ * sources' buffers), wait for the returned rows, combine.
  * Caller-given topk_ids outside [0, num_experts) are not sent anywhere (their slots add nothing
  * to ``out``) and record PRISM_MOE_ERR_ARG in the workspace's error word. When a wait for other
  * ranks runs out, PRISM_MOE_ERR_TIMEOUT is recorded there, the rest of that step does nothing
@@ -311,9 +312,10 @@ int prism_moe_ep_forward_norm(const void* x, const void* router_logits, const in
  * ``stream``). ``stats`` receives 8 uint64 values: [0] the step's epoch, [1] the workspace's
  * epoch counter, [2] and [3] %globaltimer ns when the first dispatch chunk was claimed and when
  * the last one was stored, [4] and [5] when the fused expert launch's first CTA started and its
- * last CTA finished, [6] rows sent to other ranks, [7] rows received from other ranks (each is
- * returned to its source after the down GEMM). Row bytes = hidden * 2. The reference has no
- * equivalent; this feeds the all-to-all bandwidth a benchmark reports.
+ * last CTA finished, [6] token rows this rank pulled from other ranks over NVLink (one per token
+ * and rank, however many of this rank's experts the token chose), [7] rows this rank returned
+ * to other ranks after the down GEMM (one per routed entry). Row bytes = hidden * 2. The
+ * reference has no equivalent; this feeds the all-to-all bandwidth a benchmark reports.
  */
 int prism_moe_ep_read_stats(const void* workspace, uint64_t* stats, void* stream);
 

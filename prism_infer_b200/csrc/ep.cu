@@ -6,26 +6,29 @@
 // Every rank owns one "landing zone" (cudaMalloc, mapped by all peers through CUDA IPC) with
 // identical offsets on every rank:
 //   flags   [2 phases][W] u64   phase A counts ready, C outputs landed; slot s is written
-//                               (st.release.sys) by source rank s with the step's epoch
-//   arrive  [2][El+W] u32       per-parity arrival counters: rows landed in each own-expert
-//                               segment (El) and from each other source (W); release adds by
-//                               the senders' copy warps, reset one step ahead by the owner
-//   counts  [2][W][E] i32       per-parity all-gathered expert histograms (row = source rank)
-//   recv    [2][W*Tmax*k][H]    rows routed to this rank's experts, in W*El segments ordered by
-//                               expected arrival (ep_counts_kernel)
+//                               (st.release) by source rank s with the step's epoch
+//   counts  [2][W][E+1] i32     per-parity all-gathered expert histograms (row = source rank;
+//                               element E = the source's token count)
+//   src_x   [Tmax][H]           this rank's token rows of the step, which the owners pull
+//   src_ids [Tmax*k] i64        this rank's expert ids of the step
+//   src_row [Tmax*k] i32        this rank's plan: expert-major row of each routed entry
+//   recv    [2][W*Tmax*k][H]    rows routed to this rank's experts, written by its own copy
+//                               warps, W*El segments ordered by slot (ep_counts_kernel)
 //   back    [2][Tmax*k][H]      this rank's expert outputs, written by the owners' down GEMM
-// Parity = epoch & 1. Double-buffering plus the per-step flag waits make reuse safe: a rank
-// can only reach step i+2's writes into a peer's parity-(i&1) buffers after it has seen that
-// peer's C flag of step i+1, which the peer raises only after its gate_up GEMM of step i+1 and
-// therefore after it finished reading step i's buffers.
+// Parity = epoch & 1. The src_* buffers are single: an owner reads them during its expert launch
+// of step i, and this rank writes them again only at step i+1, after it has seen every owner's C
+// flag of step i (raised after that launch). recv/back double-buffering plus the per-step flag
+// waits make their reuse safe: a rank can only reach step i+2's stores into a peer's
+// parity-(i&1) back buffer after it has seen that peer's C flag of step i+1.
 //
-// Step (prism_moe_ep_forward): route -> plan -> counts all-gather (A) and tables -> one fused
-// expert launch (expert_fused_sm100.cu) whose copy warps dispatch the rows into the owners'
-// recv buffers (per-segment arrival counters) while its producer waits only for the segment
-// each gate_up tile reads, and whose down epilogue stores every output row into its source
-// rank's back buffer; its last CTA signals C -> wait C -> local combine.
-// Every wait is bounded (prism_moe_set_wait_limits; 10 s by default); a wait that runs out
-// records PRISM_MOE_ERR_TIMEOUT, and the later kernels of that step then do nothing (their
+// Step (prism_moe_ep_forward): route (ids into src_ids) -> plan (rows into src_row) -> copy x
+// into src_x -> counts all-gather (A) and tables -> one fused expert launch
+// (expert_fused_sm100.cu) whose copy warps fill the receive buffer (own rows first, then each
+// source's rows pulled over NVLink, one token row per token and rank) while its producer waits
+// only for the counter of the segment each gate_up tile reads, and whose down epilogue stores
+// every output row into its source rank's back buffer; its last CTA signals C -> wait C -> local
+// combine. Every wait is bounded (prism_moe_set_wait_limits; 10 s by default); a wait that runs
+// out records PRISM_MOE_ERR_TIMEOUT, and the later kernels of that step then do nothing (their
 // tables may describe rows that never arrive).
 //
 // Epoch. The step's epoch (the flag value; its parity picks the buffers) lives in the workspace
@@ -33,6 +36,10 @@
 // 0, by incrementing the workspace's counter — and every later kernel of the step reads it there.
 // With the device counter no launch argument changes from step to step, so a step can be
 // captured once in a CUDA graph and replayed.
+//
+// Scopes. A system-scope fence costs microseconds (more while host copies run); a GPU-scope one
+// about half a microsecond. Only the flag exchange, the owners' first read of the sources' rows
+// and the return of outputs use system scope; every arrival counter is this GPU's own.
 #include <algorithm>
 #include <cstring>
 
@@ -44,13 +51,11 @@ namespace {
 
 constexpr int kMaxRanks = 64;
 constexpr int kMaxExperts = 1024;
-// flags (2 x 64 x 8 B, padded to 4 KB) + arrival counters (2 x (1024 + 64) x 4 B); zero at
-// allocation
-constexpr size_t kHeaderBytes = 4096 + 2 * (kMaxExperts + kMaxRanks) * sizeof(uint32_t);
-constexpr size_t kCountsMaxBytes = sizeof(int32_t) * 2 * kMaxRanks * kMaxExperts;
+constexpr size_t kFlagBytes = 4096;   // 2 x 64 x 8 B flags, padded; zero at allocation
+constexpr size_t kCountsMaxBytes = sizeof(int32_t) * 2 * kMaxRanks * (kMaxExperts + 1);
 
 struct Landing {
-  size_t flags, arrive, counts, recv, back, total;
+  size_t flags, counts, src_x, src_ids, src_row, recv, back, total;
   int64_t rcap;       // rows of one recv parity
   int64_t bcap;       // rows of one back parity
 };
@@ -59,10 +64,15 @@ Landing landing_layout(int W, int64_t max_tokens, int k, int64_t H, int E, int64
   Landing L{};
   size_t o = 0;
   L.flags = o;
-  L.arrive = 4096;
-  o += kHeaderBytes;
+  o += kFlagBytes;
   L.counts = o;
-  o += align_up(sizeof(int32_t) * 2 * W * E, 256);
+  o += align_up(sizeof(int32_t) * 2 * W * (E + 1), 256);
+  L.src_x = o;
+  o += align_up(static_cast<size_t>(max_tokens * H * es), 256);
+  L.src_ids = o;
+  o += align_up(sizeof(int64_t) * max_tokens * k, 256);
+  L.src_row = o;
+  o += align_up(sizeof(int32_t) * max_tokens * k, 256);
   L.rcap = static_cast<int64_t>(W) * max_tokens * k;
   L.bcap = max_tokens * k;
   L.recv = o;
@@ -74,8 +84,8 @@ Landing landing_layout(int W, int64_t max_tokens, int k, int64_t H, int E, int64
 }
 
 struct EpWs {
-  size_t err, ids, w, plan, plan_bytes, counts, offsets, entry_row, row_entry, seg_offsets,
-      seg_expert, seg_base, dst_base, src_rows, flag_c, done, h, total;
+  size_t err, w, plan, plan_bytes, counts, offsets, row_entry, seg_offsets, seg_expert, seg_base,
+      seg_src_row, src_tokens, chunk_base, arrive, flag_c, done, h, total;
 };
 
 EpWs ep_ws_layout(int64_t max_tokens, int64_t H, int64_t I, int E, int k, int W, int64_t rcap,
@@ -88,20 +98,20 @@ EpWs ep_ws_layout(int64_t max_tokens, int64_t H, int64_t I, int E, int k, int W,
     o += align_up(bytes > 0 ? bytes : 1, 256);
     return at;
   };
-  L.err = take(256);
-  L.ids = take(sizeof(int64_t) * N);
+  L.err = take(256);                                  // + EpStepState at kEpStepOffset
   L.w = take(es * N);
   L.plan_bytes = dispatch_workspace_size(N, E, 1);
   L.plan = take(L.plan_bytes);
   L.counts = take(sizeof(int32_t) * E);
   L.offsets = take(sizeof(int32_t) * (E + 1));
-  L.entry_row = take(sizeof(int32_t) * N);
   L.row_entry = take(sizeof(int32_t) * N);
   L.seg_offsets = take(sizeof(int32_t) * (E + 1));   // W * El receive segments
   L.seg_expert = take(sizeof(int32_t) * E);
   L.seg_base = take(sizeof(uint64_t) * E);
-  L.dst_base = take(sizeof(int32_t) * E);
-  L.src_rows = take(sizeof(int32_t) * W);
+  L.seg_src_row = take(sizeof(int32_t) * E);
+  L.src_tokens = take(sizeof(int32_t) * W);
+  L.chunk_base = take(sizeof(int32_t) * (W + 1));
+  L.arrive = take(sizeof(uint32_t) * (E + W));       // El + W used
   L.flag_c = take(sizeof(uint64_t) * W);
   L.done = take(sizeof(unsigned int) * 4);   // chunk claim, chunks stored, CTAs done
   L.h = take(expert_scratch_bytes(rcap, I, es));
@@ -149,28 +159,29 @@ __device__ int32_t block_excl_scan(int32_t v, int n, int32_t* tmp, int32_t* tota
   return incl - (i < n ? v : 0);
 }
 
-// Phase A: all-gather the expert histograms, then derive this step's tables.
+// Phase A: all-gather the expert histograms and token counts, then derive this step's tables.
 //
-// Receive layout on rank d: W * El segments in expected-arrival order. Segment (j, le), index
-// j * El + le, holds the rows of local expert le sent by source (d - j) mod W, in the source's
-// expert-major order. Source s writes to destinations in the order s, s+1, ... (mod W), so the
-// rows it sends to d arrive j = (d - s) mod W slots into its sequence, and d's GEMM reads the
-// segments of the sources that are done first.
+// Receive layout on rank d: W * El segments in slot order. Segment (j, le), index j * El + le,
+// holds the rows of local expert le of source (d - j) mod W, in the source's expert-major
+// order. Slot 0 is d's own rows, copied first; the copy warps then pull slot 1, 2, ... in order,
+// so d's GEMM reads the segments that are complete first.
 struct CountsArgs {
   const int32_t* my_counts;   // [E] this rank's expert histogram
+  int64_t my_tokens;          // this rank's token count
   const uint64_t* peers;      // [W] landing zones
   size_t flags_off, counts_off;
   size_t back_off, back_stride;       // parity-0 returned-rows buffer, bytes per parity
-  size_t arrive_off, arrive_stride;   // parity-0 arrival counters, bytes per parity
   int64_t row_bytes;
-  int W, me, E;
+  int W, me, E, k;
   uint64_t host_epoch;        // 0: take the next value of the workspace's counter
   EpStepState* step;
   int32_t* seg_offsets;       // [W*El + 1]
   int32_t* seg_expert;        // [W*El]
-  uint64_t* seg_base;         // [W*El]
-  int32_t* dst_base;          // [E]
-  int32_t* src_rows;          // [W] rows received in slot j, from source (me - j) mod W
+  uint64_t* seg_base;         // [W*El] return address of each segment's first row
+  int32_t* seg_src_row;       // [W*El] source-side expert-major row of each segment's first row
+  int32_t* src_tokens;        // [W] token count of the source in slot j
+  int32_t* chunk_base;        // [W+1] first copy chunk of slot j
+  unsigned int* arrive;       // [El+W] arrival counters, zeroed here
   uint64_t* flag_c;           // [W]
   unsigned int* claim;        // [0] chunk claim, [1] chunks stored
   int* err;
@@ -187,6 +198,7 @@ __global__ void __launch_bounds__(1024) ep_counts_kernel(const CountsArgs a) {
   const size_t flags_off = a.flags_off, counts_off = a.counts_off;
   const int W = a.W, me = a.me, E = a.E;
   const int El = E / W;
+  const int CE = E + 1;                            // counts row stride
   int* err = a.err;
   // 0. this step's epoch, and the step's statistics reset
   if (threadIdx.x == 0) {
@@ -198,6 +210,7 @@ __global__ void __launch_bounds__(1024) ep_counts_kernel(const CountsArgs a) {
     st->disp_t1 = 0;
     st->fused_t0 = ~0ull;
     st->fused_t1 = 0;
+    st->send_rows = 0;
     s_epoch = e;
   }
   __syncthreads();
@@ -205,17 +218,13 @@ __global__ void __launch_bounds__(1024) ep_counts_kernel(const CountsArgs a) {
   const int par = static_cast<int>(epoch & 1);
   const size_t back_off = a.back_off + static_cast<size_t>(par) * a.back_stride;
   const int64_t row_bytes = a.row_bytes;
-  int32_t* __restrict__ seg_offsets = a.seg_offsets;
-  int32_t* __restrict__ seg_expert = a.seg_expert;
-  uint64_t* __restrict__ seg_base = a.seg_base;
-  int32_t* __restrict__ dst_base = a.dst_base;
-  // 1. my histogram into row `me` of every rank's counts[par]
-  for (int i = threadIdx.x; i < W * E; i += blockDim.x) {
-    const int d = i / E, e = i % E;
-    int32_t* dst = reinterpret_cast<int32_t*>(peers[d] + counts_off) + (par * W + me) * E;
-    dst[e] = my_counts[e];
+  // 1. my histogram and token count into row `me` of every rank's counts[par]
+  for (int i = threadIdx.x; i < W * CE; i += blockDim.x) {
+    const int d = i / CE, e = i % CE;
+    int32_t* dst = reinterpret_cast<int32_t*>(peers[d] + counts_off) + (par * W + me) * CE;
+    dst[e] = e < E ? my_counts[e] : static_cast<int32_t>(a.my_tokens);
   }
-  threadfence_scoped(W > 1);
+  threadfence_scoped(W > 1);   // also publishes src_x / src_ids / src_row written before this
   __syncthreads();
   if (threadIdx.x < W)
     store_release_scoped(flag_addr(peers[threadIdx.x], flags_off, W, 0, me), epoch, W > 1);
@@ -225,54 +234,48 @@ __global__ void __launch_bounds__(1024) ep_counts_kernel(const CountsArgs a) {
   __syncthreads();
   __threadfence();
   const volatile int32_t* C =
-      reinterpret_cast<const volatile int32_t*>(peers[me] + counts_off) + par * W * E;
+      reinterpret_cast<const volatile int32_t*>(peers[me] + counts_off) + par * W * CE;
   const int i = threadIdx.x;
   // 3. my receive segments
   int32_t v = 0;
   if (i < E) {
     const int j = i / El, le = i % El;
-    v = C[((me - j + W) % W) * E + me * El + le];
+    v = C[((me - j + W) % W) * CE + me * El + le];
   }
   const int32_t seg_ex = block_excl_scan(v, E, tmp, &total);
   if (i < E) {
-    seg_offsets[i] = seg_ex;
-    seg_expert[i] = i % El;
+    a.seg_offsets[i] = seg_ex;
+    a.seg_expert[i] = i % El;
   }
-  if (i == 0) seg_offsets[E] = total;
+  if (i == 0) a.seg_offsets[E] = total;
   // 4. rows per (destination, source) pair
   for (int p = i; p < W * W; p += blockDim.x) {
     const int d = p / W, s = p % W;
     int32_t r = 0;
-    for (int le = 0; le < El; ++le) r += C[s * E + d * El + le];
+    for (int le = 0; le < El; ++le) r += C[s * CE + d * El + le];
     R[p] = r;
   }
   __syncthreads();
-  if (i == 0) {   // rows that cross NVLink this step, each way
-    uint64_t send = 0, recv = 0;
-    for (int d = 0; d < W; ++d)
-      if (d != me) {
-        send += static_cast<uint64_t>(R[d * W + me]);
-        recv += static_cast<uint64_t>(R[me * W + d]);
-      }
-    a.step->send_rows = send;
-    a.step->recv_rows = recv;
+  if (i == 0) {
+    uint64_t back = 0;   // rows this rank's down GEMM returns to other ranks
+    for (int s = 0; s < W; ++s)
+      if (s != me) back += static_cast<uint64_t>(R[me * W + s]);
+    a.step->recv_rows = back;
+    // copy chunks: slot 0 in 32-row chunks of this rank's own rows, then slot j >= 1 in chunks
+    // of 32 / k tokens of its source
+    const int tpc = 32 / a.k;
+    int32_t cb = 0;
+    a.chunk_base[0] = 0;
+    cb += (R[me * W + me] + 31) / 32;
+    a.chunk_base[1] = cb;
+    for (int j = 1; j < W; ++j) {
+      cb += (C[((me - j + W) % W) * CE + E] + tpc - 1) / tpc;
+      a.chunk_base[j + 1] = cb;
+    }
   }
-  if (i < W) a.src_rows[i] = R[me * W + (me - i + W) % W];
-  // 5. where my rows of expert e start in its owner's receive layout
-  const int32_t mine = i < E ? C[me * E + i] : 0;
-  const int32_t my_ex = block_excl_scan(mine, E, tmp, nullptr);
-  if (i < E) tmp[i] = my_ex;
-  __syncthreads();
-  if (i < E) {
-    const int d = i / El;
-    const int jd = (d - me + W) % W;
-    int32_t base = my_ex - tmp[d * El];
-    for (int j = 0; j < jd; ++j) base += R[d * W + (d - j + W) % W];
-    dst_base[i] = base;
-  }
-  __syncthreads();
-  // 6. return address of each segment's first row: its source's back buffer, at the source's
-  //    expert-major row of its first row for my expert le
+  if (i < W) a.src_tokens[i] = C[((me - i + W) % W) * CE + E];
+  // 5. return address of each segment's first row (its source's back buffer, at the source's
+  //    expert-major row of its first row for my expert le) and that row itself.
   //    One warp per source rank scans that source's histogram 32 experts at a time.
   {
     const int lane = i & 31;
@@ -281,29 +284,28 @@ __global__ void __launch_bounds__(1024) ep_counts_kernel(const CountsArgs a) {
       int32_t carry = 0;
       for (int base = 0; base < (me + 1) * El; base += 32) {
         const int e = base + lane;
-        const int32_t c = e < E ? C[s * E + e] : 0;
+        const int32_t c = e < E ? C[s * CE + e] : 0;
         int32_t incl = c;
 #pragma unroll
         for (int off = 1; off < 32; off <<= 1) {
           const int32_t y = __shfl_up_sync(0xffffffffu, incl, off);
           if (lane >= off) incl += y;
         }
-        if (e >= me * El && e < (me + 1) * El)
-          seg_base[j * El + (e - me * El)] =
+        if (e >= me * El && e < (me + 1) * El) {
+          const int32_t first = carry + incl - c;
+          a.seg_src_row[j * El + (e - me * El)] = first;
+          a.seg_base[j * El + (e - me * El)] =
               peers[s] + back_off +
-              static_cast<uint64_t>(carry + incl - c) * static_cast<uint64_t>(row_bytes);
+              static_cast<uint64_t>(first) * static_cast<uint64_t>(row_bytes);
+        }
         carry += __shfl_sync(0xffffffffu, incl, 31);
       }
     }
   }
-  // 7. where this rank announces C (outputs landed) on each peer. The dispatch's chunk counter
-  //    starts at zero, and so do the next step's arrival counters (the other parity: every row
-  //    of the previous step was consumed by this rank's previous gate_up, and no peer adds to
-  //    the next step's before it has seen this rank's next A flag).
-  uint32_t* next_arrive = reinterpret_cast<uint32_t*>(
-      peers[me] + a.arrive_off + static_cast<size_t>(par ^ 1) * a.arrive_stride);
+  // 6. this step's copy counters start at zero; where this rank announces C (outputs landed)
+  //    on each peer
   if (i < 2) a.claim[i] = 0u;
-  for (int c = i; c < El + W; c += blockDim.x) next_arrive[c] = 0u;
+  for (int c = i; c < El + W; c += blockDim.x) a.arrive[c] = 0u;
   threadfence_scoped(W > 1);
   if (i < W) a.flag_c[i] = reinterpret_cast<uint64_t>(flag_addr(peers[i], flags_off, W, 1, me));
 }
@@ -346,9 +348,9 @@ __attribute__((visibility("default"))) int prism_moe_ep_alloc_landing(size_t byt
   PRISM_CHECK_ARG(bytes > 0 && ptr && ipc_handle, "ep_alloc_landing: bad arguments");
   void* p = nullptr;
   PRISM_CUDA(cudaMalloc(&p, bytes));
-  // flags at epoch 0, arrival counters at 0, and the all-gathered histograms at 0 (so that a
-  // step whose counts exchange timed out never derives tables from uninitialised memory)
-  cudaError_t e = cudaMemset(p, 0, std::min(bytes, kHeaderBytes + kCountsMaxBytes));
+  // flags at epoch 0 and the all-gathered histograms at 0 (so that a step whose counts exchange
+  // timed out never derives tables from uninitialised memory)
+  cudaError_t e = cudaMemset(p, 0, std::min(bytes, kFlagBytes + kCountsMaxBytes));
   if (e == cudaSuccess) {
     cudaIpcMemHandle_t h;
     e = cudaIpcGetMemHandle(&h, p);
@@ -429,71 +431,77 @@ __attribute__((visibility("default"))) int prism_moe_ep_forward_norm(
                   "ep_forward: workspace too small (%zu < %zu)", workspace_bytes, L.total);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(workspace);
+  char* land = static_cast<char*>(my_landing);
   int* err = reinterpret_cast<int*>(ws + L.err);
   EpStepState* step = reinterpret_cast<EpStepState*>(ws + kEpStepOffset);
   const int64_t T = num_tokens;
+  // this step's ids and plan go straight into the landing zone, where the owners read them
+  int64_t* ids = reinterpret_cast<int64_t*>(land + LL.src_ids);
+  int32_t* entry_row = reinterpret_cast<int32_t*>(land + LL.src_row);
   record_stage(0, st);
-  const int64_t* ids = topk_ids_in;
   const void* w = topk_weights_in;
   if (router_logits) {
-    ids = reinterpret_cast<int64_t*>(ws + L.ids);
     w = ws + L.w;
-    int r = route_topk(router_logits, dtype, T, E, k, renorm, const_cast<int64_t*>(ids),
-                       const_cast<void*>(w), nullptr, st);
+    int r = route_topk(router_logits, dtype, T, E, k, renorm, ids, const_cast<void*>(w), nullptr,
+                       st);
     if (r) return r;
+  } else if (T > 0) {
+    PRISM_CUDA(cudaMemcpyAsync(ids, topk_ids_in, sizeof(int64_t) * T * k,
+                               cudaMemcpyDeviceToDevice, st));
   }
   int32_t* counts = reinterpret_cast<int32_t*>(ws + L.counts);
   int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
-  int32_t* entry_row = reinterpret_cast<int32_t*>(ws + L.entry_row);
   int32_t* row_entry = reinterpret_cast<int32_t*>(ws + L.row_entry);
   record_stage(1, st);
   // ids outside [0, E) (caller-given) are left out of the plan and recorded as ERR_ARG in the
-  // step's error word; no row is sent for them and their slots add nothing to the output
+  // step's error word; no row is copied for them and their slots add nothing to the output
   int r = build_plan(ids, T, k, E, 1, nullptr, nullptr, nullptr, counts, offsets, entry_row,
                      row_entry, ws + L.plan, L.plan_bytes, st, err);
   if (r) return r;
+  if (T > 0)   // this step's token rows, where the owners pull them from
+    PRISM_CUDA(cudaMemcpyAsync(land + LL.src_x, x, static_cast<size_t>(T * hidden * es),
+                               cudaMemcpyDeviceToDevice, st));
   record_stage(2, st);   // counts all-gather and the step's tables
   int32_t* seg_offsets = reinterpret_cast<int32_t*>(ws + L.seg_offsets);
   int32_t* seg_expert = reinterpret_cast<int32_t*>(ws + L.seg_expert);
   uint64_t* seg_base = reinterpret_cast<uint64_t*>(ws + L.seg_base);
-  int32_t* dst_base = reinterpret_cast<int32_t*>(ws + L.dst_base);
   uint64_t* flag_c = reinterpret_cast<uint64_t*>(ws + L.flag_c);
   unsigned int* done = reinterpret_cast<unsigned int*>(ws + L.done);
-  char* land = static_cast<char*>(my_landing);
   const size_t recv_stride = static_cast<size_t>(LL.rcap) * hidden * es;
   const size_t back_stride = static_cast<size_t>(LL.bcap) * hidden * es;
-  const size_t arrive_stride = static_cast<size_t>(El + W) * sizeof(uint32_t);
 
   CountsArgs ca{};
   ca.my_counts = counts;
+  ca.my_tokens = T;
   ca.peers = peer_landing;
   ca.flags_off = LL.flags;
   ca.counts_off = LL.counts;
   ca.back_off = LL.back;
   ca.back_stride = back_stride;
-  ca.arrive_off = LL.arrive;
-  ca.arrive_stride = arrive_stride;
   ca.row_bytes = hidden * es;
   ca.W = W;
   ca.me = me;
   ca.E = E;
+  ca.k = k;
   ca.host_epoch = epoch;
   ca.step = step;
   ca.seg_offsets = seg_offsets;
   ca.seg_expert = seg_expert;
   ca.seg_base = seg_base;
-  ca.dst_base = dst_base;
-  ca.src_rows = reinterpret_cast<int32_t*>(ws + L.src_rows);
+  ca.seg_src_row = reinterpret_cast<int32_t*>(ws + L.seg_src_row);
+  ca.src_tokens = reinterpret_cast<int32_t*>(ws + L.src_tokens);
+  ca.chunk_base = reinterpret_cast<int32_t*>(ws + L.chunk_base);
+  ca.arrive = reinterpret_cast<unsigned int*>(ws + L.arrive);
   ca.flag_c = flag_c;
   ca.claim = done;
   ca.err = err;
   ca.peer_wait_ns = peer_wait_limit_ns();
   ep_counts_kernel<<<1, 1024, 0, st>>>(ca);
   PRISM_LAUNCH_CHECK("ep_counts_kernel launch");
-  // One launch per GPU for the rest of the exchange and the experts: its copy warps dispatch
-  // this rank's rows into the owners' receive buffers while its producer waits only for the
-  // segment the next gate_up tile reads; the down epilogue stores every output row into its
-  // source rank's back buffer, and the last CTA signals C.
+  // One launch per GPU for the rest of the exchange and the experts: its copy warps fill the
+  // receive buffer (own rows, then every source's rows pulled over NVLink) while its producer
+  // waits only for the counter of the segment the next gate_up tile reads; the down epilogue
+  // stores every output row into its source rank's back buffer, and the last CTA signals C.
   GemmDispatch disp{};
   disp.x = x;
   disp.vpr = hidden * es / 16;
@@ -502,14 +510,16 @@ __attribute__((visibility("default"))) int prism_moe_ep_forward_norm(
   disp.ids = ids;
   disp.row_entry = row_entry;
   disp.expert_offsets = offsets;
-  disp.dst_base = dst_base;
-  disp.src_rows = reinterpret_cast<int32_t*>(ws + L.src_rows);
   disp.peers = peer_landing;
-  for (int p = 0; p < 2; ++p) {
-    disp.recv_off[p] = LL.recv + p * recv_stride;
-    disp.arrive_off[p] = LL.arrive + p * arrive_stride;
-    disp.x_recv[p] = land + disp.recv_off[p];
-  }
+  disp.src_x_off = LL.src_x;
+  disp.src_ids_off = LL.src_ids;
+  disp.src_row_off = LL.src_row;
+  disp.seg_offsets = seg_offsets;
+  disp.seg_src_row = ca.seg_src_row;
+  disp.src_tokens = ca.src_tokens;
+  disp.chunk_base = ca.chunk_base;
+  disp.arrive = ca.arrive;
+  for (int p = 0; p < 2; ++p) disp.x_recv[p] = land + LL.recv + p * recv_stride;
   disp.epoch_ptr = &step->epoch;
   disp.claim = done;
   disp.step = step;

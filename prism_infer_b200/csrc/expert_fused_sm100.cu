@@ -13,14 +13,16 @@
 // claimed in stream order by CTAs that are running and every dependency points to an earlier
 // claim, so the launch makes progress even when the GPU holds fewer CTAs than the grid.
 //
-// With expert parallelism (``GemmDispatch``) four more warps per CTA dispatch this rank's
-// expert-major rows into the owners' receive buffers inside the same launch: 32-row chunks
-// claimed from a shared counter, peers in rotated order, each run of one expert's rows
-// published on the owner's per-segment arrival counter (release, system scope); the producer
-// of a gate_up tile waits for its segment's counter. The down epilogue stores every output row
-// straight into its source rank's buffer (GemmOutput::seg_base, 128-byte segments over NVLink),
-// so both transfers overlap tensor-core work. (Forwarding the outputs through the copy warps
-// instead, staged in local memory, measured slower at 2 and 4 GPUs.)
+// With expert parallelism (``GemmDispatch``) four more warps per CTA fill this rank's receive
+// buffer inside the same launch, in chunks claimed from a shared counter: first this rank's own
+// rows (expert-major, published per expert segment), then, source by source, the rows other
+// ranks routed here, PULLED over NVLink from the sources' landing zones one token row per
+// (token, rank) however many of this rank's experts the token chose (the de-duplicated
+// dispatch); every count lands on a counter in this GPU's memory at GPU scope, and the producer
+// of a gate_up tile waits for the counter of its segment. The down epilogue stores every output
+// row straight into its source rank's buffer (GemmOutput::seg_base, 128-byte segments over
+// NVLink), so both transfers overlap tensor-core work. (Forwarding the outputs through the copy
+// warps instead, staged in local memory, measured slower at 2 and 4 GPUs.)
 //
 // Warp roles: warp 0 lane 0 claims tiles, publishes each to a shared-memory ring (8 entries,
 // full/empty mbarriers) and issues the TMA loads; warp 1 lane 0 issues the MMAs; warps 2..5
@@ -109,38 +111,15 @@ __device__ __forceinline__ void add_release_gpu(unsigned int* p, uint32_t v) {
 // ---------------------------------------------------------------------------------------------
 // copy warps (expert parallelism)
 // ---------------------------------------------------------------------------------------------
-// Rows per dispatch chunk (one lane looks up each row): the unit copy warps claim, and at most
-// one publish per arrival counter inside it.
+// Rows per own-slot chunk (one lane looks up each row).
 constexpr int kChunkRows = 32;
 
-// Arrival counter (on the owner) that a row for expert ``e`` counts on. The owner's receive slot
-// j = (d - me) mod W holds this rank's rows; slot 0 (this rank's own experts, copied first) has
-// one counter per local expert so the GEMM can start on the first segments, counters 0..El-1;
-// every other slot has one counter for the whole slot, counter El + j, so that an owner does
-// one system-scope acquire per source and CTA rather than one per segment.
-__device__ __forceinline__ int arrival_counter(const GemmDispatch& D, int64_t e, int d) {
-  return d == D.me ? static_cast<int>(e - static_cast<int64_t>(d) * D.El)
-                   : D.El + (d - D.me + D.W) % D.W;
-}
-
-// Dispatch: ``n`` rows for owner ``d`` are written; publish them on the owner's arrival counter
-// ``ctr``. The warp barrier orders every lane's stores before lane 0's release add
-// (cumulative). Rows for this rank's own experts are published at GPU scope: a system-scope
-// release also waits for this GPU's traffic to the host (copies running beside the step), which
-// an owner on the same GPU does not need.
-__device__ __forceinline__ void dispatch_flush(const GemmDispatch& D, size_t arrive_off, int ctr,
-                                               unsigned int n, int lane) {
+// Add ``n`` to this GPU's arrival counter ``ctr``: the warp barrier orders every lane's row stores
+// before lane 0's release add (cumulative, GPU scope: writer and reader are both on this GPU).
+__device__ __forceinline__ void arrival_add(const GemmDispatch& D, int ctr, unsigned int n,
+                                            int lane) {
   __syncwarp();
-  if (lane == 0) {
-    const int d = ctr < D.El ? D.me : (D.me + ctr - D.El) % D.W;
-    uint32_t* counter = reinterpret_cast<uint32_t*>(D.peers[d] + arrive_off) + ctr;
-    if (d == D.me) {
-      add_release_gpu_u32(counter, n);
-    } else {
-      __threadfence_system();
-      add_release_sys(counter, n);
-    }
-  }
+  if (lane == 0) add_release_gpu_u32(D.arrive + ctr, n);
   __syncwarp();
 }
 
@@ -165,28 +144,27 @@ __device__ __forceinline__ void copy_row_pair(const uint4* sa, uint4* da, const 
   }
 }
 
-// One dispatch chunk (kChunkRows rows) of this rank's expert-major rows [0, n), own block first and then
-// the following ranks' blocks. Lanes look up the chunk's rows at once; rows then move in pairs.
-// Every row below n belongs to an entry with a valid expert id (the plan leaves the others out),
-// so every store lands inside an owner's receive buffer.
-__device__ void dispatch_chunk(const GemmDispatch& D, int64_t c, int64_t n, int par, int lane) {
-  const int64_t shift = D.expert_offsets[D.me * D.El];
+// Slot 0: chunk ``c`` of this rank's own expert-major rows for its own experts. Every row below
+// the plan's count belongs to an entry with a valid expert id (the plan leaves the others out),
+// so every store lands inside the receive buffer.
+__device__ void own_chunk(const GemmDispatch& D, int64_t c, uint8_t* recv, int lane) {
+  const int e0 = D.me * D.El;
+  const int64_t base = D.expert_offsets[e0];
+  const int64_t n = D.expert_offsets[e0 + D.El] - base;
   const int64_t i0 = c * kChunkRows;
   const int nr = static_cast<int>(n - i0 < kChunkRows ? n - i0 : kChunkRows);
   const uint4* x = static_cast<const uint4*>(D.x);
-  const size_t recv_off = D.recv_off[par], arrive_off = D.arrive_off[par];
-  int my_ctr = -1;
+  int my_le = -1;
   int64_t my_src = 0;
   uint64_t my_dst = 0;
   if (lane < nr) {
-    const int64_t q = (i0 + lane + shift) % n;
+    const int64_t q = base + i0 + lane;
     const int32_t f = D.row_entry[q];
     const int64_t e = D.ids[f];
     my_src = f / D.k;
-    const int d = static_cast<int>(e / D.El);
-    my_ctr = arrival_counter(D, e, d);
-    const int64_t dst_row = D.dst_base[e] + (q - D.expert_offsets[e]);
-    my_dst = D.peers[d] + recv_off + static_cast<uint64_t>(dst_row * D.vpr * 16);
+    my_le = static_cast<int>(e - e0);
+    const int64_t dst_row = D.seg_offsets[my_le] + (q - D.expert_offsets[e]);
+    my_dst = reinterpret_cast<uint64_t>(recv) + static_cast<uint64_t>(dst_row * D.vpr * 16);
   }
   int c_run = -1;
   unsigned int n_run = 0;
@@ -198,39 +176,119 @@ __device__ void dispatch_chunk(const GemmDispatch& D, int64_t c, int64_t n, int 
                   x + __shfl_sync(0xffffffffu, my_src, rb) * D.vpr,
                   reinterpret_cast<uint4*>(__shfl_sync(0xffffffffu, my_dst, rb)), two, D.vpr,
                   lane);
-    // runs of one arrival counter; a run's rows are all stored before its count is published
+    // runs of one expert; a run's rows are all stored before its count is published
     for (int t = r; t <= rb; ++t) {
-      const int ctr = __shfl_sync(0xffffffffu, my_ctr, t);
-      if (ctr != c_run) {
-        if (n_run) dispatch_flush(D, arrive_off, c_run, n_run, lane);
-        c_run = ctr;
+      const int le = __shfl_sync(0xffffffffu, my_le, t);
+      if (le != c_run) {
+        if (n_run) arrival_add(D, c_run, n_run, lane);
+        c_run = le;
         n_run = 0;
       }
       ++n_run;
     }
   }
-  if (n_run) dispatch_flush(D, arrive_off, c_run, n_run, lane);
+  if (n_run) arrival_add(D, c_run, n_run, lane);
 }
 
-// Copy-warp loop: claim dispatch chunks until none are left. The rows to send are the
-// plan's valid rows, expert_offsets[E] of them. The warp that claims the first chunk and the
-// warp that stores the last one stamp the step's dispatch window.
+// Read one token row from a peer (over NVLink; L2-only loads, so nothing stale comes from L1)
+// and write it to the receive rows of the lanes in ``mask`` (their addresses in ``my_dst``).
+__device__ __forceinline__ void pull_row(const uint4* src, uint32_t mask, uint64_t my_dst,
+                                         int64_t vpr, int lane) {
+  constexpr int kVec = 8;
+  for (int64_t v0 = 0; v0 < vpr; v0 += 32 * kVec) {
+    uint4 a[kVec];
+#pragma unroll
+    for (int u = 0; u < kVec; ++u) {
+      const int64_t v = v0 + lane + 32 * u;
+      if (v < vpr) a[u] = __ldcg(src + v);
+    }
+    for (uint32_t m = mask; m; m &= m - 1) {
+      uint4* dst = reinterpret_cast<uint4*>(__shfl_sync(0xffffffffu, my_dst, __ffs(m) - 1));
+#pragma unroll
+      for (int u = 0; u < kVec; ++u) {
+        const int64_t v = v0 + lane + 32 * u;
+        if (v < vpr) dst[v] = a[u];
+      }
+    }
+  }
+}
+
+// Slots j >= 1: chunk ``c`` of source s = (me - j) mod W, tokens [t0, t0 + nt), one lane per
+// routed entry (lane = token * k + slot). A lane whose entry chose one of this rank's experts
+// reads the entry's expert-major row on s and derives its receive row; each token row then
+// crosses NVLink once for all of this rank's experts it chose. Returns the rows read.
+__device__ unsigned int pull_chunk(const GemmDispatch& D, int j, int64_t t0, int nt,
+                                   uint8_t* recv, int lane) {
+  const int s = (D.me - j + D.W) % D.W;
+  const uint64_t base = D.peers[s];
+  const int64_t* ids = reinterpret_cast<const int64_t*>(base + D.src_ids_off);
+  const int32_t* rows = reinterpret_cast<const int32_t*>(base + D.src_row_off);
+  const uint4* x = reinterpret_cast<const uint4*>(base + D.src_x_off);
+  const int e0 = D.me * D.El;
+  bool mine = false;
+  uint64_t my_dst = 0;
+  if (lane < nt * D.k) {
+    const int64_t f = t0 * D.k + lane;
+    const int64_t e = __ldcg(ids + f);
+    mine = e >= e0 && e < e0 + D.El;   // ids outside [0, E) are never this rank's
+    if (mine) {
+      const int seg = j * D.El + static_cast<int>(e - e0);
+      const int64_t q = __ldcg(rows + f);
+      const int64_t dst_row = D.seg_offsets[seg] + (q - D.seg_src_row[seg]);
+      my_dst = reinterpret_cast<uint64_t>(recv) + static_cast<uint64_t>(dst_row * D.vpr * 16);
+    }
+  }
+  const uint32_t any = __ballot_sync(0xffffffffu, mine);
+  const uint32_t tok_bits = D.k == 32 ? 0xffffffffu : ((1u << D.k) - 1u);
+  unsigned int pulled = 0;
+  for (int u = 0; u < nt; ++u) {
+    const uint32_t mask = any & (tok_bits << (u * D.k));
+    if (!mask) continue;
+    pull_row(x + (t0 + u) * D.vpr, mask, my_dst, D.vpr, lane);
+    ++pulled;
+  }
+  return pulled;
+}
+
+// Copy-warp loop: claim chunks (own slot first, then the sources in slot order) until none are
+// left. The warp that claims the first chunk and the warp that stores the last one stamp the
+// step's dispatch window; rows pulled over NVLink are counted into the step's statistics.
 __device__ void copy_warp_loop(const GemmDispatch& D, int par, int lane) {
-  const int64_t n = D.expert_offsets[D.E];
-  const int64_t nchunks = (n + kChunkRows - 1) / kChunkRows;
+  uint8_t* recv = static_cast<uint8_t*>(const_cast<void*>(D.x_recv[par]));
+  const int64_t total = D.chunk_base[D.W];
+  const int64_t own = D.chunk_base[1];
+  const int tpc = 32 / D.k;                       // tokens per pull chunk
+  bool fenced = false;
+  unsigned long long pulled = 0;
   for (;;) {
     unsigned int claimed = 0;
     if (lane == 0) claimed = atomicAdd(D.claim, 1u);
     const int64_t c = __shfl_sync(0xffffffffu, claimed, 0);
-    if (c >= nchunks) break;
+    if (c >= total) break;
     if (c == 0 && lane == 0 && D.step) D.step->disp_t0 = global_timer_ns();
-    dispatch_chunk(D, c, n, par, lane);
+    if (c < own) {
+      own_chunk(D, c, recv, lane);
+    } else {
+      if (!fenced) {   // acquire (system scope) of the peers' rows, once per warp
+        fence_acq_rel_sys();
+        fenced = true;
+      }
+      int j = 1;
+      while (j + 1 < D.W && D.chunk_base[j + 1] <= c) ++j;
+      const int64_t t0 = (c - D.chunk_base[j]) * tpc;
+      const int64_t Ts = D.src_tokens[j];
+      const int nt = static_cast<int>(Ts - t0 < tpc ? Ts - t0 : tpc);
+      pulled += pull_chunk(D, j, t0, nt, recv, lane);
+      arrival_add(D, D.El + j, static_cast<unsigned int>(nt), lane);
+    }
     if (lane == 0) {
       const unsigned int stored = atomicAdd(D.claim + 1, 1u);
-      if (stored + 1 == static_cast<unsigned int>(nchunks) && D.step)
+      if (stored + 1 == static_cast<unsigned int>(total) && D.step)
         D.step->disp_t1 = global_timer_ns();
     }
   }
+  if (lane == 0 && pulled && D.step)
+    atomicAdd(reinterpret_cast<unsigned long long*>(&D.step->send_rows), pulled);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -322,9 +380,6 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
     int ready_key = -1;      // dispatch: the last arrival counter seen complete
     int32_t ready_mt = -1;   // every h row of this m-tile is stored
     bool ok = true;
-    const uint32_t* my_arrive =
-        kDispatch ? reinterpret_cast<const uint32_t*>(disp.peers[disp.me] + disp.arrive_off[par])
-                  : nullptr;
     for (;;) {
       int32_t t = -1;
       {
@@ -356,15 +411,14 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
         if (kDispatch && key > ready_key) {
           const uint32_t need =
               static_cast<uint32_t>(j == 0 ? P.seg_offsets[s + 1] - P.seg_offsets[s]
-                                           : disp.src_rows[j]);
-          while (load_relaxed_sys(my_arrive + key) != need) {
+                                           : disp.src_tokens[j]);
+          while (load_relaxed_sys(disp.arrive + key) != need) {
             if (*abort || global_timer_ns() - t0 > P.peer_wait_ns) {
               ok = false;
               break;
             }
           }
-          // acquire: the source's rows before the counter it raised (slot 0 is this GPU itself)
-          fence_acq_rel_scoped(j > 0);
+          fence_acq_rel_gpu();   // acquire: the copy warps' rows before the count they added
           // rows written through the generic proxy (peer stores), read next by TMA
           asm volatile("fence.proxy.async.global;" ::: "memory");
           ready_key = key;

@@ -18,8 +18,8 @@ struct EpStepState {
   uint64_t counter;             // last epoch issued on this rank
   uint64_t disp_t0, disp_t1;    // %globaltimer ns: first dispatch chunk claimed, last one stored
   uint64_t fused_t0, fused_t1;  // %globaltimer ns: fused expert launch, first CTA in, last out
-  uint64_t send_rows;           // rows this rank sends to other ranks (dispatch, remote only)
-  uint64_t recv_rows;           // rows other ranks send here (returned to them by the down GEMM)
+  uint64_t send_rows;           // token rows this rank pulled from other ranks (dispatch)
+  uint64_t recv_rows;           // rows this rank returned to other ranks (down GEMM outputs)
 };
 constexpr size_t kEpStepOffset = 64;   // inside the workspace's first 256-byte block
 
@@ -39,34 +39,44 @@ struct GemmOutput {
   bool remote = false;           // rows or flags may live on other GPUs: system-scope fences
 };
 
-// Expert-parallel exchange carried out INSIDE the fused expert launch (ep.cu): extra copy warps
-// write this rank's expert-major rows into the owners' receive buffers, peers in rotated order
-// starting with this rank itself, and after each run of rows for one arrival counter add the
-// run's length to it on the owner. The receive layout on rank d is segment (j, le), index
-// j * El + le = rows of local expert le from source (d - j) mod W. Arrival counters: one per
-// segment of slot 0 (the owner's own rows, counters 0..El-1) and one per later slot (counter
-// El + j, all rows from that source). The GEMM's producer waits (bounded) until the counter of
-// the segment a tile reads equals its row count (slot 0) or src_rows[j]. Every per-parity field
-// is indexed by ``*epoch_ptr & 1``.
-// Only rows [0, expert_offsets[E]) are sent: entries with an expert id outside [0, E) have no
-// row (the dispatch plan leaves them out) and are never copied anywhere.
+// Expert-parallel exchange carried out INSIDE the fused expert launch (ep.cu), by four extra
+// copy warps per CTA that fill this rank's receive buffer. Its layout: W * El segments, segment
+// (j, le), index j * El + le = rows of local expert le from source (me - j) mod W, in the
+// source's expert-major order ("slot" j). Two kinds of work, claimed as one sequence of chunks:
+//   * slot 0, this rank's own rows (chunks [0, chunk_base[1])): 32 expert-major rows per chunk,
+//     copied from ``x``; after each run of one expert the run's length is added to arrival
+//     counter le;
+//   * slots j >= 1 (chunks [chunk_base[j], chunk_base[j+1])): the rows are PULLED from source s
+//     over NVLink, ``32 / k`` tokens per chunk: the warp reads the tokens' expert ids and plan
+//     rows from s's landing zone, and reads each token row once however many of this rank's
+//     experts it chose, writing one copy per chosen expert (one NVLink row per token and rank:
+//     the de-duplicated dispatch). After each chunk its token count is added to arrival counter
+//     El + j.
+// All arrival counters live in this GPU's memory and are written by this GPU's warps, so both
+// the counts and the producer's acquire are GPU-scope. The GEMM's producer waits (bounded) until
+// the counter of the segment a tile reads is complete: the segment's rows (slot 0) or the
+// source's token count (slots j >= 1). Per-parity fields are indexed by ``*epoch_ptr & 1``.
 struct GemmDispatch {
-  const void* x = nullptr;              // [T, H] this rank's token rows
+  const void* x = nullptr;              // [T, H] this rank's token rows (slot 0 source)
   int64_t vpr = 0;                      // 16-byte vectors per row
   int k = 1;
   int E = 1;                            // experts in total (W * El)
-  const int64_t* ids = nullptr;         // [T*k] expert of each flat entry
-  const int32_t* row_entry = nullptr;   // [T*k] expert-major row -> flat entry
-  const int32_t* expert_offsets = nullptr;   // [E+1]
-  const int32_t* dst_base = nullptr;    // [E] first row of my expert-e rows in the owner's layout
-  const int32_t* src_rows = nullptr;    // [W] rows this rank receives in slot j (all its segments)
+  const int64_t* ids = nullptr;         // [T*k] this rank's expert id of each flat entry
+  const int32_t* row_entry = nullptr;   // [T*k] this rank's expert-major row -> flat entry
+  const int32_t* expert_offsets = nullptr;   // [E+1] this rank's expert-major offsets
   const uint64_t* peers = nullptr;      // [W] landing-zone base addresses
+  size_t src_x_off = 0;                 // every landing zone: [T_max, H] token rows
+  size_t src_ids_off = 0;               //                     [T_max*k] int64 expert ids
+  size_t src_row_off = 0;               //                     [T_max*k] int32 expert-major rows
+  const int32_t* seg_offsets = nullptr; // [W*El+1] this rank's receive layout
+  const int32_t* seg_src_row = nullptr; // [W*El] source-side expert-major row of a segment's row 0
+  const int32_t* src_tokens = nullptr;  // [W] tokens of the source in slot j
+  const int32_t* chunk_base = nullptr;  // [W+1] first chunk of slot j (chunk_base[W] = total)
+  unsigned int* arrive = nullptr;       // [El+W] arrival counters (zeroed by ep_counts_kernel)
   const void* x_recv[2] = {nullptr, nullptr};   // this rank's receive buffers (GEMM A operand)
-  size_t recv_off[2] = {0, 0};          // byte offsets of the receive buffers in a landing zone
-  size_t arrive_off[2] = {0, 0};        // byte offsets of the [W*El] u32 arrival counters
   const uint64_t* epoch_ptr = nullptr;  // the step's epoch (EpStepState::epoch)
-  unsigned int* claim = nullptr;        // [0] next dispatch chunk to copy, [1] chunks stored
-  EpStepState* step = nullptr;          // dispatch timing, or NULL
+  unsigned int* claim = nullptr;        // [0] next chunk to copy, [1] chunks stored
+  EpStepState* step = nullptr;          // dispatch timing and rows pulled, or NULL
   const int* gate_err = nullptr;        // the launch does nothing when this holds ERR_TIMEOUT
   int W = 1, me = 0, El = 1;
 };
