@@ -190,24 +190,36 @@ __device__ void own_chunk(const GemmDispatch& D, int64_t c, uint8_t* recv, int l
   if (n_run) arrival_add(D, c_run, n_run, lane);
 }
 
-// Read one token row from a peer (over NVLink; L2-only loads, so nothing stale comes from L1)
-// and write it to the receive rows of the lanes in ``mask`` (their addresses in ``my_dst``).
-__device__ __forceinline__ void pull_row(const uint4* src, uint32_t mask, uint64_t my_dst,
-                                         int64_t vpr, int lane) {
+// Read one or two token rows from a peer (over NVLink; L2-only loads, so nothing stale comes
+// from L1), both in flight at once, and write each to the receive rows of the lanes in its mask
+// (their addresses in ``my_dst``).
+__device__ __forceinline__ void pull_row_pair(const uint4* sa, uint32_t ma, const uint4* sb,
+                                              uint32_t mb, uint64_t my_dst, int64_t vpr,
+                                              int lane) {
   constexpr int kVec = 8;
+  const bool two = mb != 0;
   for (int64_t v0 = 0; v0 < vpr; v0 += 32 * kVec) {
-    uint4 a[kVec];
+    uint4 a[kVec], b[kVec];
 #pragma unroll
     for (int u = 0; u < kVec; ++u) {
       const int64_t v = v0 + lane + 32 * u;
-      if (v < vpr) a[u] = __ldcg(src + v);
+      if (v < vpr) a[u] = __ldcg(sa + v);
+      if (two && v < vpr) b[u] = __ldcg(sb + v);
     }
-    for (uint32_t m = mask; m; m &= m - 1) {
+    for (uint32_t m = ma; m; m &= m - 1) {
       uint4* dst = reinterpret_cast<uint4*>(__shfl_sync(0xffffffffu, my_dst, __ffs(m) - 1));
 #pragma unroll
       for (int u = 0; u < kVec; ++u) {
         const int64_t v = v0 + lane + 32 * u;
         if (v < vpr) dst[v] = a[u];
+      }
+    }
+    for (uint32_t m = mb; m; m &= m - 1) {
+      uint4* dst = reinterpret_cast<uint4*>(__shfl_sync(0xffffffffu, my_dst, __ffs(m) - 1));
+#pragma unroll
+      for (int u = 0; u < kVec; ++u) {
+        const int64_t v = v0 + lane + 32 * u;
+        if (v < vpr) dst[v] = b[u];
       }
     }
   }
@@ -240,12 +252,18 @@ __device__ unsigned int pull_chunk(const GemmDispatch& D, int j, int64_t t0, int
   }
   const uint32_t any = __ballot_sync(0xffffffffu, mine);
   const uint32_t tok_bits = D.k == 32 ? 0xffffffffu : ((1u << D.k) - 1u);
-  unsigned int pulled = 0;
-  for (int u = 0; u < nt; ++u) {
-    const uint32_t mask = any & (tok_bits << (u * D.k));
-    if (!mask) continue;
-    pull_row(x + (t0 + u) * D.vpr, mask, my_dst, D.vpr, lane);
-    ++pulled;
+  uint32_t todo = 0;   // bit u: token u chose one of this rank's experts
+  for (int u = 0; u < nt; ++u)
+    if (any & (tok_bits << (u * D.k))) todo |= 1u << u;
+  const unsigned int pulled = __popc(todo);
+  while (todo) {       // two token rows in flight per pass
+    const int ua = __ffs(todo) - 1;
+    todo &= todo - 1;
+    const int ub = todo ? __ffs(todo) - 1 : ua;
+    const uint32_t mb = todo ? any & (tok_bits << (ub * D.k)) : 0u;
+    if (todo) todo &= todo - 1;
+    pull_row_pair(x + (t0 + ua) * D.vpr, any & (tok_bits << (ua * D.k)), x + (t0 + ub) * D.vpr,
+                  mb, my_dst, D.vpr, lane);
   }
   return pulled;
 }
