@@ -13,8 +13,9 @@ prism_infer/engine/parallel/expert_parallel.py, on B200 kernels.
 
 Transports. ``p2p`` (the default for bf16 on CUDA) runs the whole step in the library's
 ``prism_moe_ep_forward``: a device-side counts all-gather, then one fused expert launch whose
-copy warps write the rows into the owners' CUDA-IPC-mapped receive buffers and whose down
-epilogue writes the outputs back into the sources' buffers — no host synchronisation. ``nccl``
+copy warps fill this rank's receive buffer — pulling the rows other ranks routed here from their
+CUDA-IPC-mapped landing zones, one row per (token, rank) — and whose down epilogue writes the
+outputs back into the sources' buffers — no host synchronisation. ``nccl``
 keeps the reference's structure (all_to_all_single with a host read of the split sizes) around
 the library's kernels, with the layout below.
 
@@ -155,9 +156,10 @@ class ExpertParallelMoE(ExpertBank):
     def forward_p2p(self, x: torch.Tensor, router_logits=None, topk_ids=None, topk_weights=None,
                     top_k: int | None = None, renorm: bool = True, residual=None,
                     norm_weight=None, eps: float = 1e-6):
-        """One step over NVLink peer memory: route (from logits, or given ids/weights), dispatch
-        into the owners' landing zones, grouped experts, outputs stored back into the sources'
-        landing zones by the down GEMM, combine. Collective over the EP group.
+        """One step over NVLink peer memory: route (from logits, or given ids/weights), rows
+        pulled by their experts' owners (one per token and owner), grouped experts, outputs
+        stored back into the sources' landing zones by the down GEMM, combine. Collective over
+        the EP group.
 
         The step's epoch is counted on the device (epoch argument 0), so after the first call
         (which reserves the landing zones, a collective that allocates) a step can be captured in
