@@ -24,7 +24,8 @@ Reported:
   combine_weighted_sum) on the same routing;
 * ``cfg3`` / ``cfg4``: benchmark configs 3 (Zipf-skewed routing, T=4096/rank) and 4
   (Qwen3-235B-A22B block, H=4096, I=1536, T=16384/rank) at the same EP size, each with its own
-  parity; ``decode_cfg1``: config 1 (T=64, single GPU) at N=1, HBM roofline;
+  parity; ``decode_cfg1``: config 1's batch (T=64 per rank) eager and replayed from a CUDA graph,
+  against the HBM roofline of the expert weights it streams;
 * ``a2a`` (N>1): NVLink bytes each rank sends per step, the dispatch window stamped inside the
   fused launch (%globaltimer) and the bandwidths they give;
 * ``cpu_baseline``: the numpy restatement of the reference's CPU path on a bounded sample of the
@@ -653,25 +654,31 @@ def run_ours(args):
     else:
         extra["a2a"] = a2a_stats(moe, x, world)
 
-    # ---- config 1 decode (T=64) at N=1 ----
-    if world == 1 and not args.no_decode:
+    # ---- config 1 decode (T=64 per rank) ----
+    # At N=1 the whole step streams the experts' weights (HBM roofline); at N>1 the same batch
+    # runs through the expert-parallel step. Both eager and replayed from a CUDA graph captured
+    # once (the EP epoch is counted on the device, so the captured step replays as is).
+    if not args.no_decode:
         xd = x[:64].contiguous()
 
         def dec(_i):
             with torch.inference_mode():
                 moe(xd)
-        ms_dec = time_device(dec, 200, 20, 1)
+        ms_dec = time_device(dec, 200, 20, world)
         with torch.inference_mode():
             _, ids, _ = moe.route(xd)
-        n_exp = int(torch.unique(ids).numel())
+        hit = reduce_over_ranks(torch.bincount(ids.reshape(-1), minlength=E).float().tolist(),
+                                "sum", world)
+        El = E // world
+        n_exp = sum(1 for e in range(rank * El, (rank + 1) * El) if hit[e] > 0)
+        n_exp = int(reduce_over_ranks([float(n_exp)], "max", world)[0])
         wbytes = n_exp * 3 * H * I * 2
         t_step = ms_dec / 200 / 1e3
-        extra["decode_cfg1"] = {"tokens": 64, "ms_per_step": ms_dec / 200,
-                                "tokens_per_s": 64 / t_step,
-                                "weight_bytes_per_step": wbytes,
+        extra["decode_cfg1"] = {"tokens_per_rank": 64, "ms_per_step": ms_dec / 200,
+                                "tokens_per_s": world * 64 / t_step,
+                                "weight_bytes_per_step_per_rank": wbytes,
                                 "hbm_gbs": wbytes / t_step / 1e9,
                                 "frac_of_hbm_peak": wbytes / t_step / 1e9 / hbm_peak}
-        # the same step captured once in a CUDA graph and replayed (no host work per step)
         side = torch.cuda.Stream(device)
         side.wait_stream(torch.cuda.current_stream(device))
         with torch.cuda.stream(side), torch.inference_mode():
@@ -681,9 +688,12 @@ def run_ours(args):
         graph = torch.cuda.CUDAGraph()
         with torch.inference_mode(), torch.cuda.graph(graph):
             moe(xd)
-        ms_g = time_device(lambda _i: graph.replay(), 200, 20, 1)
+        ms_g = time_device(lambda _i: graph.replay(), 200, 20, world)
         extra["decode_cfg1"]["graph_ms_per_step"] = ms_g / 200
+        extra["decode_cfg1"]["graph_tokens_per_s"] = world * 64 / (ms_g / 200 / 1e3)
         extra["decode_cfg1"]["graph_hbm_gbs"] = wbytes / (ms_g / 200 / 1e3) / 1e9
+        extra["decode_cfg1"]["device_error_ranks"] = int(reduce_over_ranks(
+            [float(check_device_error(moe, world, device) != 0)], "sum", world)[0])
         del graph
 
     if world == 1 and not args.no_ep1:

@@ -150,3 +150,71 @@ def test_ep_full_size(W, case, skew):
         assert d.max() <= BF16_MAX_ABS, (r, d.max())
         assert d.mean() / np.abs(ref).mean() <= BF16_MEAN_REL
         assert np.array_equal(res[r]["out"], res[r]["out2"])
+
+
+def _graph_worker(rank, W, port, outdir):
+    sys.path.insert(0, str(REPO))
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from prism_infer_b200.engine.parallel import set_expert_parallel_size
+    from prism_infer_b200.layers.moe import MoE
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=W, timeout=timedelta(seconds=120),
+                            device_id=dev)
+    set_expert_parallel_size(W)
+    H, E, k, I, T = 512, 64, 8, 256, 96
+    torch.manual_seed(1234)                       # same weights on every rank
+    moe = MoE(H, I, E, k)
+    with torch.no_grad():
+        moe.gate.weight.normal_(0, 0.02)
+        moe.ep_moe.w_gate_up.normal_(0, H ** -0.5)
+        moe.ep_moe.w_down.normal_(0, I ** -0.5)
+    moe = moe.to(dev, torch.bfloat16)
+    gen = torch.Generator(device=dev).manual_seed(rank)
+    xs = [torch.randn(T, H, generator=gen, device=dev).to(torch.bfloat16) for _ in range(3)]
+    x_in = xs[0].clone()
+    ok = True
+    with torch.inference_mode():
+        eager = [moe(x) for x in xs]              # the first call reserves the landing zones
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            moe(x_in)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            y = moe(x_in)
+        for _ in range(2):
+            for x, ref in zip(xs, eager):
+                x_in.copy_(x)
+                graph.replay()
+                torch.cuda.synchronize()
+                ok = ok and torch.equal(y, ref)
+    moe.ep_moe.check_device_error()
+    del graph
+    Path(outdir, f"r{rank}").write_text("ok" if ok else "mismatch")
+    moe.ep_moe.release()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_ep_step_replays_from_cuda_graph():
+    """An expert-parallel step captured once in a CUDA graph on every rank and replayed with new
+    inputs gives the eager outputs bit for bit (the step's epoch is counted on the device;
+    prism_infer/engine/model_runner.py:281-318 captures decode steps the same way)."""
+    W = 2
+    if torch.cuda.device_count() < W:
+        pytest.skip(f"needs {W} GPUs")
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_graph_worker, args=(W, port, d), nprocs=W, join=True,
+                           start_method="spawn")
+        assert [Path(d, f"r{r}").read_text() for r in range(W)] == ["ok"] * W
