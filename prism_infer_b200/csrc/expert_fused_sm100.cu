@@ -190,36 +190,26 @@ __device__ void own_chunk(const GemmDispatch& D, int64_t c, uint8_t* recv, int l
   if (n_run) arrival_add(D, c_run, n_run, lane);
 }
 
-// Read one or two token rows from a peer (over NVLink; L2-only loads, so nothing stale comes
-// from L1), both in flight at once, and write each to the receive rows of the lanes in its mask
-// (their addresses in ``my_dst``).
-__device__ __forceinline__ void pull_row_pair(const uint4* sa, uint32_t ma, const uint4* sb,
-                                              uint32_t mb, uint64_t my_dst, int64_t vpr,
-                                              int lane) {
+// Read one token row from a peer (over NVLink; L2-only loads, so nothing stale comes from L1)
+// and write it to the receive rows of the lanes in ``mask`` (their addresses in ``my_dst``).
+// (Two rows in flight per pass needed 64 more registers per thread and spilled; one row keeps
+// 8 vectors per lane in flight.)
+__device__ __forceinline__ void pull_row(const uint4* src, uint32_t mask, uint64_t my_dst,
+                                         int64_t vpr, int lane) {
   constexpr int kVec = 8;
-  const bool two = mb != 0;
   for (int64_t v0 = 0; v0 < vpr; v0 += 32 * kVec) {
-    uint4 a[kVec], b[kVec];
+    uint4 a[kVec];
 #pragma unroll
     for (int u = 0; u < kVec; ++u) {
       const int64_t v = v0 + lane + 32 * u;
-      if (v < vpr) a[u] = __ldcg(sa + v);
-      if (two && v < vpr) b[u] = __ldcg(sb + v);
+      if (v < vpr) a[u] = __ldcg(src + v);
     }
-    for (uint32_t m = ma; m; m &= m - 1) {
+    for (uint32_t m = mask; m; m &= m - 1) {
       uint4* dst = reinterpret_cast<uint4*>(__shfl_sync(0xffffffffu, my_dst, __ffs(m) - 1));
 #pragma unroll
       for (int u = 0; u < kVec; ++u) {
         const int64_t v = v0 + lane + 32 * u;
         if (v < vpr) dst[v] = a[u];
-      }
-    }
-    for (uint32_t m = mb; m; m &= m - 1) {
-      uint4* dst = reinterpret_cast<uint4*>(__shfl_sync(0xffffffffu, my_dst, __ffs(m) - 1));
-#pragma unroll
-      for (int u = 0; u < kVec; ++u) {
-        const int64_t v = v0 + lane + 32 * u;
-        if (v < vpr) dst[v] = b[u];
       }
     }
   }
@@ -252,18 +242,12 @@ __device__ unsigned int pull_chunk(const GemmDispatch& D, int j, int64_t t0, int
   }
   const uint32_t any = __ballot_sync(0xffffffffu, mine);
   const uint32_t tok_bits = D.k == 32 ? 0xffffffffu : ((1u << D.k) - 1u);
-  uint32_t todo = 0;   // bit u: token u chose one of this rank's experts
-  for (int u = 0; u < nt; ++u)
-    if (any & (tok_bits << (u * D.k))) todo |= 1u << u;
-  const unsigned int pulled = __popc(todo);
-  while (todo) {       // two token rows in flight per pass
-    const int ua = __ffs(todo) - 1;
-    todo &= todo - 1;
-    const int ub = todo ? __ffs(todo) - 1 : ua;
-    const uint32_t mb = todo ? any & (tok_bits << (ub * D.k)) : 0u;
-    if (todo) todo &= todo - 1;
-    pull_row_pair(x + (t0 + ua) * D.vpr, any & (tok_bits << (ua * D.k)), x + (t0 + ub) * D.vpr,
-                  mb, my_dst, D.vpr, lane);
+  unsigned int pulled = 0;
+  for (int u = 0; u < nt; ++u) {
+    const uint32_t mask = any & (tok_bits << (u * D.k));
+    if (!mask) continue;
+    pull_row(x + (t0 + u) * D.vpr, mask, my_dst, D.vpr, lane);
+    ++pulled;
   }
   return pulled;
 }
@@ -506,7 +490,16 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
         rphase ^= 1;
       }
       if (t < 0) break;
-      const int nkb = tile_at(t, M, P.n_gu, P.n_dn, P.lag).kind == 0 ? P.kb_gu : P.kb_dn;
+      const TileRef tr = tile_at(t, M, P.n_gu, P.n_dn, P.lag);
+      const int nkb = tr.kind == 0 ? P.kb_gu : P.kb_dn;
+      uint32_t idesc = F::kIdesc;
+      {   // a segment's last m-tile with <= 64 rows: M=64 MMAs
+        const int s = find_segment(prefix, P.nseg, tr.mt);
+        const int32_t row0 = P.seg_offsets[s] + (tr.mt - prefix[s]) * 128;
+        const int32_t seg_end = P.seg_offsets[s + 1];
+        if (half_tile((seg_end < P.rows_cap ? seg_end : P.rows_cap) - row0))
+          idesc = idesc_bf16_f32(kHalfRows, kBN);
+      }
       const int buf = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait_bounded(&acc_empty[buf], acc_phase ^ 1, abort, P.wait_ns)) {
@@ -526,7 +519,7 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk)
           tc_mma_bf16(d_tmem, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32),
-                      F::kIdesc, (kb | kk) != 0 ? 1u : 0u);
+                      idesc, (kb | kk) != 0 ? 1u : 0u);
         tc_commit(&empty[stage]);
         if (++stage == F::kStages) {
           stage = 0;
@@ -551,7 +544,6 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
   } else if (warp >= 2) {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
-    const int row_in_tile = q * 32 + lane;  // row within the tile
     uint8_t* stage_out = smem + F::kStageOutOffset + (warp - 2) * 32 * kStageRowBytes;
     int rslot = 0;
     uint32_t rphase = 0;
@@ -583,6 +575,8 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
       }
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * kBN;
+      // row within the tile held by this lane (half tiles: lanes 0-15 of a quarter)
+      const int row_in_tile = tile_row_of_lane(half_tile(rows_valid), q, lane);
       const bool has_row = row_in_tile < rows_valid;
       const int64_t row = row0 + row_in_tile;
       if (tr.kind == 0) {

@@ -174,6 +174,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + buf * kBN;
+      uint32_t idesc = C::kIdesc;
+      if constexpr (!kPair) {   // a segment's last m-tile with <= 64 rows: M=64 MMAs
+        const int32_t mt = static_cast<int32_t>(tile / num_n_tiles);
+        const int s = find_segment(prefix, nseg, mt);
+        const int32_t row0 = seg_offsets[s] + (mt - prefix[s]) * C::kRows;
+        const int32_t seg_end = seg_offsets[s + 1];
+        if (half_tile((seg_end < rows_cap ? seg_end : rows_cap) - row0))
+          idesc = idesc_bf16_f32(kHalfRows, kBN);
+      }
       for (int kb = 0; kb < num_kb; ++kb) {
         if (!mbar_wait_bounded(&full[stage], phase, abort, kWaitNs)) {
           ok = false;
@@ -189,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if constexpr (kPair)
             tc_mma_bf16_pair(d_tmem, ad, bd, C::kIdesc, acc);
           else
-            tc_mma_bf16(d_tmem, ad, bd, C::kIdesc, acc);
+            tc_mma_bf16(d_tmem, ad, bd, idesc, acc);
         }
         if constexpr (kPair)
           tc_commit_pair(&empty[stage], 0x3);
@@ -221,7 +230,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= 2) {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
-    const int row_in_tile = q * 32 + lane;  // row within this CTA's 128 rows
     uint8_t* stage_out = smem + C::kStageOutOffset + (warp - 2) * 32 * kStageRowBytes;
     const uint32_t acc_empty_leader =
         kPair ? mapa_shared(smem_u32(&acc_empty[0]), 0) : smem_u32(&acc_empty[0]);
@@ -235,6 +243,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int32_t row0 = seg_offsets[s] + (mt - prefix[s]) * C::kRows + 128 * rank;
       const int32_t seg_end = seg_offsets[s + 1];
       const int32_t rows_valid = (seg_end < rows_cap ? seg_end : rows_cap) - row0;
+      // row within this CTA's 128 rows held by this lane (half tiles: lanes 0-15 of a quarter)
+      const int row_in_tile = tile_row_of_lane(!kPair && half_tile(rows_valid), q, lane);
       if (!mbar_wait_bounded(&acc_full[buf], acc_phase, abort, kWaitNs)) {
         *abort = 1;
         record_device_error(err, PRISM_MOE_ERR_TIMEOUT);

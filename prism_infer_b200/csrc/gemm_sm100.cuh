@@ -40,6 +40,18 @@ struct Cfg {
 
 enum : int { kGateUp = 0, kDown = 1 };
 
+// Half tiles. A segment's last m-tile that holds at most 64 valid rows runs M=64 MMAs (half the
+// tensor-core time of M=128; the TMA copy still brings 128 rows, of which the MMA reads the
+// first 64). The single-CTA M=64 accumulator uses the first 16 TMEM lanes of each 32-lane
+// quarter: tile row 16 q + i lives in lane 32 q + i (i < 16), column n in column n — CUTLASS's
+// "half subpartitions" layout (cute/atom/mma_traits_sm100.hpp, UMMA_1SM M=64). An epilogue warp
+// of quarter q therefore drains rows 16 q .. 16 q + 15 from its lanes 0..15.
+constexpr int32_t kHalfRows = 64;
+__device__ __forceinline__ bool half_tile(int32_t rows_valid) { return rows_valid <= kHalfRows; }
+__device__ __forceinline__ int tile_row_of_lane(bool half, int q, int lane) {
+  return half ? (lane < 16 ? q * 16 + lane : 1 << 30) : q * 32 + lane;
+}
+
 // Two fp32 values -> packed bf16x2 (round to nearest even) in one instruction; lo in bits 0-15.
 __device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
   uint32_t r;

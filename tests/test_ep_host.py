@@ -129,3 +129,93 @@ def test_ep_host_logic_reproduces_reference_ep(name):
         ref_recv = np.bincount(g[f"r{r}_recv_eid"], minlength=res[r]["recv_counts"].shape[1])
         assert (res[r]["recv_counts"].sum(0) == ref_recv).all()
         np.testing.assert_allclose(res[r]["out"], g[f"r{r}_out"], atol=1e-5, rtol=1e-4)
+
+
+def _receive_layout_model(ids_per_rank, E, W, k):
+    """The receive buffers the NVLink transport builds, restated on the host from the index
+    arithmetic of ep_counts_kernel (segment offsets, source rows of each segment, tokens and copy
+    chunks per slot) and of the fused launch's copy warps (own rows by plan row, other sources'
+    rows pulled token by token). Returns, per rank, an array mapping each receive row to the
+    (source rank, token) whose row it holds (-1: never written), plus the rows each rank pulls."""
+    from oracle import moe_oracle as O
+    El = E // W
+    counts = [O.expert_counts(ids, E) for ids in ids_per_rank]           # C[s][e]
+    tokens = [ids.shape[0] for ids in ids_per_rank]
+    entry_rows = []
+    for ids in ids_per_rank:                     # the source's plan: expert-major row of entry f
+        order = O.expert_major_order(ids, E)
+        er = np.empty(order.size, np.int64)
+        er[order] = np.arange(order.size)
+        entry_rows.append(er)
+    offsets = [np.concatenate([[0], np.cumsum(c)]) for c in counts]
+    layouts, pulled = [], []
+    for me in range(W):
+        seg_rows = [counts[(me - j) % W][me * El + le] for j in range(W) for le in range(El)]
+        seg_off = np.concatenate([[0], np.cumsum(seg_rows)])
+        seg_src_row = [offsets[(me - j) % W][me * El + le] for j in range(W) for le in range(El)]
+        recv = np.full(int(seg_off[-1]), -1, np.int64)
+        src_of = np.full(int(seg_off[-1]), -1, np.int64)
+        tpc = 32 // k
+        chunk_base = [0, -(-int(sum(counts[me][me * El:(me + 1) * El])) // 32)]
+        for j in range(1, W):
+            chunk_base.append(chunk_base[-1] - (-tokens[(me - j) % W] // tpc))
+        # slot 0: own rows, by expert-major plan row
+        ids, er = ids_per_rank[me], entry_rows[me]
+        for q in range(offsets[me][me * El], offsets[me][(me + 1) * El]):
+            f = int(np.nonzero(er == q)[0][0])
+            e = int(ids.reshape(-1)[f])
+            dst = seg_off[e - me * El] + (q - offsets[me][e])
+            assert recv[dst] == -1
+            recv[dst], src_of[dst] = f // k, me
+        # slots j >= 1: pulled token by token, chunks of 32 // k tokens
+        n_pulled = 0
+        for j in range(1, W):
+            s = (me - j) % W
+            n_chunks = chunk_base[j + 1] - chunk_base[j]
+            for c in range(n_chunks):
+                for t in range(c * tpc, min((c + 1) * tpc, tokens[s])):
+                    hit = False
+                    for jj in range(k):
+                        f = t * k + jj
+                        e = int(ids_per_rank[s].reshape(-1)[f])
+                        if me * El <= e < (me + 1) * El:
+                            seg = j * El + e - me * El
+                            dst = seg_off[seg] + (entry_rows[s][f] - seg_src_row[seg])
+                            assert recv[dst] == -1
+                            recv[dst], src_of[dst] = t, s
+                            hit = True
+                    n_pulled += hit
+        layouts.append((recv, src_of, seg_off))
+        pulled.append(n_pulled)
+    return layouts, pulled
+
+
+@pytest.mark.parametrize("W,k,T", [(2, 8, 67), (3, 8, 50), (4, 6, 41), (8, 8, 37), (8, 2, 9)])
+def test_pulled_receive_layout_matches_reference_order(W, k, T):
+    """The receive layout of the NVLink transport, from the kernels' index arithmetic, holds in
+    segment (slot j, local expert le) exactly the rows the reference's all_to_all delivers to
+    rank me from source (me - j) mod W for expert me*El + le, in the reference's order (flat
+    order inside an expert, expert_parallel.py:37-39), every row written once; and a token row
+    is pulled once per owner rank however many of its experts that owner holds."""
+    E = 8 * W
+    rng = np.random.default_rng(W * 100 + k)
+    ids_per_rank = [np.stack([rng.choice(E, k, replace=False) for _ in range(T + r)])
+                    for r in range(W)]
+    layouts, pulled = _receive_layout_model(ids_per_rank, E, W, k)
+    El = E // W
+    for me in range(W):
+        recv, src_of, seg_off = layouts[me]
+        assert (recv >= 0).all()
+        for j in range(W):
+            s = (me - j) % W
+            flat = ids_per_rank[s].reshape(-1)
+            for le in range(El):
+                e = me * El + le
+                want = np.nonzero(flat == e)[0] // k          # tokens, flat order
+                a, b = seg_off[j * El + le], seg_off[j * El + le + 1]
+                assert np.array_equal(recv[a:b], want)
+                assert (src_of[a:b] == s).all()
+        want_pulled = sum(int(np.any((ids_per_rank[(me - j) % W] >= me * El) &
+                                     (ids_per_rank[(me - j) % W] < (me + 1) * El), axis=1).sum())
+                          for j in range(1, W))
+        assert pulled[me] == want_pulled
