@@ -57,3 +57,24 @@ def test_argument_errors_need_no_gpu(lib):
     st = lib.prism_moe_build_dispatch_plan(None, 4, 2, 7, 4, None, None, None, None, None, None,
                                            None, 0, None)
     assert st == capi.ERR_ARG and "divisible" in capi.last_error()
+
+
+def test_controls_and_new_entry_points_check_arguments(lib):
+    # process-wide controls (no device call)
+    assert lib.prism_moe_set_expert_engine(7) == capi.ERR_ARG and "engine" in capi.last_error()
+    assert lib.prism_moe_set_expert_engine(capi.ENGINES["auto"]) == capi.OK
+    assert lib.prism_moe_set_wait_limits(-1, 0) == capi.ERR_ARG
+    assert lib.prism_moe_set_wait_limits(61_000_000_000, 0) == capi.ERR_ARG
+    assert lib.prism_moe_set_wait_limits(0, 0) == capi.OK
+    # argument checks that run before any device call
+    assert lib.prism_moe_rmsnorm(None, None, None, 1e-6, 9, 4, 64, None, None, None) == capi.ERR_ARG
+    assert lib.prism_moe_rmsnorm(None, None, None, -1.0, capi.BF16, 4, 64, None, None,
+                                 None) == capi.ERR_ARG
+    assert lib.prism_moe_ep_read_stats(None, None, None) == capi.ERR_ARG
+    epi = capi.NormEpilogue(0, 0, 1e-6, 0)     # incomplete: no residual / weight / output
+    st = lib.prism_moe_block_forward_norm(None, None, capi.BF16, 0, 64, 32, 8, 2, 1, None, None,
+                                          None, None, None, None, 1 << 20, None,
+                                          ctypes.byref(epi))
+    assert st == capi.ERR_ARG
+    assert lib.prism_moe_ep_landing_bytes(65, 8, 2, 64, 8, capi.BF16) == 0    # > 64 ranks
+    assert lib.prism_moe_ep_workspace_size(8, 64, 32, 9, 2, 2, capi.BF16) == 0   # E % W != 0
