@@ -36,6 +36,15 @@
 namespace prism {
 namespace {
 
+// Where a tile's operands start: n-tile, expert, first row of this CTA's 128 rows (before
+// finish(): the segment's first row, and the tile's index within the segment).
+struct TileLoc {
+  int nt = 0;
+  int e = 0;
+  int32_t row0 = 0;
+  int32_t mt_in_seg = 0;
+};
+
 template <int kMode, bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -107,12 +116,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t issued = 0;           // bit s: stage s has a load issued
     uint32_t issued_parity = 0;    // bit s: full-barrier parity of that load
     bool ok = true;
-    for (int64_t tile = unit; ok && tile < total_tiles; tile += num_units) {
+    // A tile's first row and expert are looked up one tile ahead: the segment search and the
+    // table loads are issued after the first k-block of the tile before it and their values
+    // used only after that tile's last k-block, so the loads overlap copies in flight instead
+    // of holding back the next tile's first copy.
+    auto lookup = [&](int64_t tile) {
+      TileLoc l;
       const int32_t mt = static_cast<int32_t>(tile / num_n_tiles);
-      const int nt = static_cast<int>(tile % num_n_tiles);
       const int s = find_segment(prefix, nseg, mt);
-      const int e = seg_expert ? seg_expert[s] : s;
-      const int32_t row0 = seg_offsets[s] + (mt - prefix[s]) * C::kRows + 128 * rank;
+      l.nt = static_cast<int>(tile % num_n_tiles);
+      l.e = s;
+      if (seg_expert) l.e = seg_expert[s];
+      l.row0 = seg_offsets[s];                          // + the tile's offset, in finish()
+      l.mt_in_seg = mt - prefix[s];
+      return l;
+    };
+    auto finish = [&](TileLoc l) {
+      l.row0 += l.mt_in_seg * C::kRows + 128 * static_cast<int32_t>(rank);
+      return l;
+    };
+    TileLoc cur;
+    if (unit < total_tiles) cur = finish(lookup(unit));
+    for (int64_t tile = unit; ok && tile < total_tiles; tile += num_units) {
+      const int nt = cur.nt, e = cur.e;
+      const int32_t row0 = cur.row0;
+      TileLoc nxt = cur;
       for (int kb = 0; kb < num_kb; ++kb) {
         if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort, kWaitNs)) {
           ok = false;
@@ -144,7 +172,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           stage = 0;
           phase ^= 1;
         }
+        if (kb == 0 && tile + num_units < total_tiles) nxt = lookup(tile + num_units);
       }
+      cur = finish(nxt);
     }
     if (!ok) {
       *abort = 1;
@@ -165,6 +195,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0;
     int it = 0;
     bool ok = true;
+    // A segment's last m-tile with <= 64 rows runs M=64 MMAs. The segment of the next tile is
+    // looked up after the first k-block of this one and the decision taken after its last, so
+    // the table loads do not delay a tile's first MMA. (x, y, z) = (segment start, segment
+    // end, the tile's first row within the segment).
+    auto lookup = [&](int64_t tile) -> int3 {
+      const int32_t mt = static_cast<int32_t>(tile / num_n_tiles);
+      const int s = find_segment(prefix, nseg, mt);
+      return make_int3(seg_offsets[s], seg_offsets[s + 1], (mt - prefix[s]) * C::kRows);
+    };
+    auto tile_idesc = [&](int3 r) -> uint32_t {
+      if constexpr (kPair) {
+        return C::kIdesc;
+      } else {
+        return half_tile((r.y < rows_cap ? r.y : rows_cap) - (r.x + r.z))
+                   ? idesc_bf16_f32(kHalfRows, kBN)
+                   : C::kIdesc;
+      }
+    };
+    uint32_t idesc = C::kIdesc;
+    if (!kPair && unit < total_tiles) idesc = tile_idesc(lookup(unit));
     for (int64_t tile = unit; ok && tile < total_tiles; tile += num_units, ++it) {
       const int buf = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
@@ -174,15 +224,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + buf * kBN;
-      uint32_t idesc = C::kIdesc;
-      if constexpr (!kPair) {   // a segment's last m-tile with <= 64 rows: M=64 MMAs
-        const int32_t mt = static_cast<int32_t>(tile / num_n_tiles);
-        const int s = find_segment(prefix, nseg, mt);
-        const int32_t row0 = seg_offsets[s] + (mt - prefix[s]) * C::kRows;
-        const int32_t seg_end = seg_offsets[s + 1];
-        if (half_tile((seg_end < rows_cap ? seg_end : rows_cap) - row0))
-          idesc = idesc_bf16_f32(kHalfRows, kBN);
-      }
+      int3 next = make_int3(0, 0, 0);
+      const bool has_next = !kPair && tile + num_units < total_tiles;
       for (int kb = 0; kb < num_kb; ++kb) {
         if (!mbar_wait_bounded(&full[stage], phase, abort, kWaitNs)) {
           ok = false;
@@ -208,12 +251,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           stage = 0;
           phase ^= 1;
         }
+        if (kb == 0 && has_next) next = lookup(tile + num_units);
       }
       if (!ok) break;
       if constexpr (kPair)
         tc_commit_pair(&acc_full[buf], 0x3);
       else
         tc_commit(&acc_full[buf]);
+      if (has_next) idesc = tile_idesc(next);
     }
     if (!ok) {
       *abort = 1;
