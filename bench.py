@@ -51,6 +51,7 @@ sys.path.insert(0, str(REPO))
 
 METRIC = "MoE-block tokens/s (Qwen3-30B-A3B block, EP=N, T=8192/rank)"
 UNIT = "tokens/s"
+NVLINK_GBS = 770.0   # measured GPU-to-GPU copy bandwidth per direction (B200, NVLink 5)
 CFGS = {
     2: dict(T=8192, H=2048, E=128, k=8, I=768, skew=False,
             name="cfg2: Qwen3-30B-A3B MoE block H=2048 E=128 top-8 I=768"),
@@ -569,49 +570,53 @@ def run_ours(args):
     # Every step copies its hidden states from pinned host memory and its output back. The
     # copies run on their own streams, double-buffered, so step i+1's upload and step i-1's
     # download overlap step i's forward (how a serving loop feeds the block).
-    x_host = [x.detach().cpu().pin_memory() for _ in range(2)]
-    y_host = [torch.empty_like(x_host[0]).pin_memory() for _ in range(2)]
-    x_dev = [torch.empty_like(x) for _ in range(2)]
-    y_dev = [torch.empty_like(x) for _ in range(2)]
-    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
-    comp = torch.cuda.current_stream(device)
-    ev_in = [torch.cuda.Event() for _ in range(2)]
-    ev_done = [torch.cuda.Event() for _ in range(2)]
-    ev_out = [torch.cuda.Event() for _ in range(2)]
-    for e in ev_done + ev_out:
-        e.record(comp)
+    # The host side of the loop runs on the CPUs nearest this GPU, so the pinned buffers
+    # sit on its NUMA node (the CPU set is put back afterwards).
+    from prism_infer_b200.engine.affinity import local_to_gpu
+    with local_to_gpu(device) as local_cpus:
+        x_host = [x.detach().cpu().pin_memory() for _ in range(2)]
+        y_host = [torch.empty_like(x_host[0]).pin_memory() for _ in range(2)]
+        x_dev = [torch.empty_like(x) for _ in range(2)]
+        y_dev = [torch.empty_like(x) for _ in range(2)]
+        s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+        comp = torch.cuda.current_stream(device)
+        ev_in = [torch.cuda.Event() for _ in range(2)]
+        ev_done = [torch.cuda.Event() for _ in range(2)]
+        ev_out = [torch.cuda.Event() for _ in range(2)]
+        for e in ev_done + ev_out:
+            e.record(comp)
 
-    def e2e_step(i, forward=True):
-        b = i % 2
-        s_in.wait_event(ev_done[b])          # x_dev[b] no longer read by step i-2
-        with torch.cuda.stream(s_in):
-            x_dev[b].copy_(x_host[b], non_blocking=True)
-            ev_in[b].record(s_in)
-        comp.wait_event(ev_in[b])
-        if forward:
-            with torch.inference_mode():
-                y = moe(x_dev[b])
-        else:
-            y = y_dev[b]
-        ev_done[b].record(comp)
-        s_out.wait_event(ev_done[b])
-        s_out.wait_event(ev_out[b])          # y_host[b] free (step i-2's copy finished)
-        with torch.cuda.stream(s_out):
-            y_host[b].copy_(y, non_blocking=True)
+        def e2e_step(i, forward=True):
+            b = i % 2
+            s_in.wait_event(ev_done[b])          # x_dev[b] no longer read by step i-2
+            with torch.cuda.stream(s_in):
+                x_dev[b].copy_(x_host[b], non_blocking=True)
+                ev_in[b].record(s_in)
+            comp.wait_event(ev_in[b])
             if forward:
-                y.record_stream(s_out)
-            ev_out[b].record(s_out)
+                with torch.inference_mode():
+                    y = moe(x_dev[b])
+            else:
+                y = y_dev[b]
+            ev_done[b].record(comp)
+            s_out.wait_event(ev_done[b])
+            s_out.wait_event(ev_out[b])          # y_host[b] free (step i-2's copy finished)
+            with torch.cuda.stream(s_out):
+                y_host[b].copy_(y, non_blocking=True)
+                if forward:
+                    y.record_stream(s_out)
+                ev_out[b].record(s_out)
 
-    def e2e_timed(forward):
-        def fn(i):
-            e2e_step(i, forward)
-            if i == steps - 1 or i < 0:
-                comp.wait_stream(s_out)
-        return fn
+        def e2e_timed(forward):
+            def fn(i):
+                e2e_step(i, forward)
+                if i == steps - 1 or i < 0:
+                    comp.wait_stream(s_out)
+            return fn
 
-    ms_e2e = time_device(e2e_timed(True), steps, max(2, warmup // 2), world)
-    e2e_value = world * T * steps / (ms_e2e / 1e3)
-    ms_copy = time_device(e2e_timed(False), steps, max(2, warmup // 2), world)
+        ms_e2e = time_device(e2e_timed(True), steps, max(2, warmup // 2), world)
+        e2e_value = world * T * steps / (ms_e2e / 1e3)
+        ms_copy = time_device(e2e_timed(False), steps, max(2, warmup // 2), world)
 
     # ---- roofline of the dominant kernel ----
     # fused engine (EP>1): both expert GEMMs in one launch, 6*H*I FLOP per routed row;
@@ -653,6 +658,21 @@ def run_ours(args):
         }
     else:
         extra["a2a"] = a2a_stats(moe, x, world)
+        # The fused launch computes and exchanges at once: its target time is the slower of its
+        # FLOPs at the tensor peak and the bytes each rank's NVLink carries per direction (rows
+        # other ranks pull from it + outputs it stores into them; by symmetry the same inbound)
+        # at the measured peer-copy bandwidth.
+        link_bytes = (extra["a2a"]["dispatch_remote_bytes_per_rank"]
+                      + extra["a2a"]["return_remote_bytes_per_rank"])
+        t_tensor = kflops / (peak * 1e12) * 1e3
+        t_link = link_bytes / (NVLINK_GBS * 1e9) * 1e3
+        roofline["fused_target"] = {
+            "bound": "nvlink" if t_link > t_tensor else "tensor",
+            "tensor_ms": t_tensor, "nvlink_ms": t_link, "target_ms": max(t_tensor, t_link),
+            "launch_ms": kms, "frac": max(t_tensor, t_link) / kms,
+            "nvlink_bytes_per_direction_per_rank": link_bytes, "link_gbs": NVLINK_GBS,
+            "link_source": "measured peer copy per direction on this pool's B200s (NVLink 5, "
+                           "900 GB/s nominal)"}
 
     # ---- config 1 decode (T=64 per rank) ----
     # At N=1 the whole step streams the experts' weights (HBM roofline); at N>1 the same batch
@@ -731,9 +751,11 @@ def run_ours(args):
                 "d2h_bytes_per_step": T * H * 2,
                 "copy_only_ms_per_step": ms_copy / steps,
                 "ms_per_step": ms_e2e / steps,
+                "host_cpus_near_gpu": local_cpus,
                 "how": "MoE.forward; per step H2D of x from pinned host and D2H of the output, "
                        "on copy streams double-buffered against the forward; copy_only: the "
-                       "same copies with no forward"},
+                       "same copies with no forward; host_cpus_near_gpu: CPUs the host loop "
+                       "and the pinned buffers were placed on (NVML affinity; null: unchanged)"},
         "gpu_launches": steps * launches_per_step(world, fused),
         "clocks": clocks,
         **extra,
