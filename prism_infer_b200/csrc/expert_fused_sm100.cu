@@ -10,10 +10,8 @@
 // is claimed L steps (several hundred tiles) after the gate_up tiles it reads. Each gate_up
 // epilogue warp publishes its stored h rows on a per-m-tile counter (release, GPU scope); the
 // producer of a down tile waits (bounded) for that counter before its TMA reads h. Tiles are
-// claimed in stream order by CTAs that are running (each up to two tiles ahead of the one it
-// works on, and through its claims in order) and every dependency points to an earlier claim:
-// the earliest unfinished claim is always being worked on and has its inputs, so the launch
-// makes progress even when the GPU holds fewer CTAs than the grid.
+// claimed in stream order by CTAs that are running and every dependency points to an earlier
+// claim, so the launch makes progress even when the GPU holds fewer CTAs than the grid.
 //
 // With expert parallelism (``GemmDispatch``) four more warps per CTA fill this rank's receive
 // buffer inside the same launch, in chunks claimed from a shared counter: first this rank's own
@@ -83,31 +81,6 @@ struct TileRef {
   int32_t mt;
   int nt;
 };
-
-// A ring entry: the claimed stream position, with kRingHalf set for a segment's last m-tile of at
-// most 64 rows (M=64 MMAs); -1 ends the stream. Positions stay below 2^30: at most
-// (2^31 / 128 + kMaxSegments) m-tiles x (n_gu + n_dn) tiles.
-constexpr int32_t kRingHalf = 1 << 30;
-
-// A claimed tile, located: its stream position (-1: none), kind and tiles, segment, expert,
-// first row and half flag. Before finish_loc(): row0 = the segment's first row, seg_end = its
-// end, and mt_rows = the tile's first row within the segment.
-struct FusedLoc {
-  int32_t t = -1;
-  TileRef tr{0, 0, 0};
-  int s = 0;
-  int e = 0;
-  int32_t row0 = 0;
-  int32_t seg_end = 0;
-  int32_t mt_rows = 0;
-  bool half = false;
-};
-
-__device__ __forceinline__ void finish_loc(FusedLoc& l, int32_t rows_cap) {
-  if (l.t < 0) return;
-  l.row0 += l.mt_rows;
-  l.half = half_tile((l.seg_end < rows_cap ? l.seg_end : rows_cap) - l.row0);
-}
 
 // Position c of the interleaved tile stream over M m-tiles.
 __device__ __forceinline__ TileRef tile_at(int32_t c, int32_t M, int nG, int nD, int L) {
@@ -409,44 +382,27 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
     int ready_key = -1;      // dispatch: the last arrival counter seen complete
     int32_t ready_mt = -1;   // every h row of this m-tile is stored
     bool ok = true;
-    // Claims and lookups run ahead: after the first k-block of tile i this thread looks up tile
-    // i+1 (claimed during tile i-1: segment search, table loads issued) and claims tile i+2;
-    // the looked-up values are used after tile i's last k-block. Neither the claim's round trip
-    // nor the table loads hold back a tile's first copy. A CTA holds at most three claims and
-    // works through them in stream order.
-    auto locate = [&](unsigned int c) {
-      FusedLoc l;
-      if (c < static_cast<unsigned int>(total)) {
-        l.t = static_cast<int32_t>(c);
-        l.tr = tile_at(l.t, M, P.n_gu, P.n_dn, P.lag);
-        l.s = find_segment(prefix, P.nseg, l.tr.mt);
-        l.e = l.s;
-        if (P.seg_expert) l.e = P.seg_expert[l.s];
-        l.row0 = P.seg_offsets[l.s];
-        l.seg_end = P.seg_offsets[l.s + 1];
-        l.mt_rows = (l.tr.mt - prefix[l.s]) * 128;
-      }
-      return l;
-    };
-    FusedLoc cur = locate(atomicAdd(P.claim, 1u));
-    finish_loc(cur, P.rows_cap);
-    unsigned int claimed = cur.t >= 0 ? atomicAdd(P.claim, 1u) : 0xffffffffu;
     for (;;) {
+      int32_t t = -1;
+      {
+        const unsigned int c = atomicAdd(P.claim, 1u);
+        if (c < static_cast<unsigned int>(total)) t = static_cast<int32_t>(c);
+      }
       if (!mbar_wait_bounded(&ring_empty[rslot], rphase ^ 1, abort, P.wait_ns)) {
         ok = false;
         break;
       }
-      ring_tile[rslot] = cur.t < 0 ? -1 : (cur.t | (cur.half ? kRingHalf : 0));
+      ring_tile[rslot] = t;
       mbar_arrive(&ring_full[rslot]);
       if (++rslot == F::kRing) {
         rslot = 0;
         rphase ^= 1;
       }
-      if (cur.t < 0) break;
-      const TileRef tr = cur.tr;
-      const int s = cur.s;
-      const int e = cur.e;
-      const int32_t row0 = cur.row0;
+      if (t < 0) break;
+      const TileRef tr = tile_at(t, M, P.n_gu, P.n_dn, P.lag);
+      const int s = find_segment(prefix, P.nseg, tr.mt);
+      const int e = P.seg_expert ? P.seg_expert[s] : s;
+      const int32_t row0 = P.seg_offsets[s] + (tr.mt - prefix[s]) * 128;
       const uint64_t t0 = global_timer_ns();
       if (tr.kind == 0) {
         // receive slot j of segment s (rows from source (me - j) mod W) and its counter: one per
@@ -480,7 +436,6 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
         ready_mt = tr.mt;
       }
       if (!ok) break;
-      FusedLoc nxt;
       const int nkb = tr.kind == 0 ? P.kb_gu : P.kb_dn;
       for (int kb = 0; kb < nkb; ++kb) {
         if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort, P.wait_ns)) {
@@ -504,14 +459,8 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
           stage = 0;
           phase ^= 1;
         }
-        if (kb == 0) {
-          nxt = locate(claimed);
-          claimed = nxt.t >= 0 ? atomicAdd(P.claim, 1u) : 0xffffffffu;
-        }
       }
       if (!ok) break;
-      finish_loc(nxt, P.rows_cap);
-      cur = nxt;
     }
     if (!ok) {
       *abort = 1;
@@ -534,17 +483,23 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
         ok = false;
         break;
       }
-      const int32_t v = ring_tile[rslot];
+      const int32_t t = ring_tile[rslot];
       mbar_arrive(&ring_empty[rslot]);
       if (++rslot == F::kRing) {
         rslot = 0;
         rphase ^= 1;
       }
-      if (v < 0) break;
-      const TileRef tr = tile_at(v & ~kRingHalf, M, P.n_gu, P.n_dn, P.lag);
+      if (t < 0) break;
+      const TileRef tr = tile_at(t, M, P.n_gu, P.n_dn, P.lag);
       const int nkb = tr.kind == 0 ? P.kb_gu : P.kb_dn;
-      // a segment's last m-tile with <= 64 rows: M=64 MMAs
-      const uint32_t idesc = (v & kRingHalf) ? idesc_bf16_f32(kHalfRows, kBN) : F::kIdesc;
+      uint32_t idesc = F::kIdesc;
+      {   // a segment's last m-tile with <= 64 rows: M=64 MMAs
+        const int s = find_segment(prefix, P.nseg, tr.mt);
+        const int32_t row0 = P.seg_offsets[s] + (tr.mt - prefix[s]) * 128;
+        const int32_t seg_end = P.seg_offsets[s + 1];
+        if (half_tile((seg_end < P.rows_cap ? seg_end : P.rows_cap) - row0))
+          idesc = idesc_bf16_f32(kHalfRows, kBN);
+      }
       const int buf = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait_bounded(&acc_empty[buf], acc_phase ^ 1, abort, P.wait_ns)) {
@@ -598,15 +553,15 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
         record_device_error(P.err, PRISM_MOE_ERR_TIMEOUT);
         break;
       }
-      const int32_t v = ring_tile[rslot];
+      const int32_t t = ring_tile[rslot];
       __syncwarp();
       if (lane == 0) mbar_arrive(&ring_empty[rslot]);
       if (++rslot == F::kRing) {
         rslot = 0;
         rphase ^= 1;
       }
-      if (v < 0) break;
-      const TileRef tr = tile_at(v & ~kRingHalf, M, P.n_gu, P.n_dn, P.lag);
+      if (t < 0) break;
+      const TileRef tr = tile_at(t, M, P.n_gu, P.n_dn, P.lag);
       const int buf = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       const int s = find_segment(prefix, P.nseg, tr.mt);
@@ -621,7 +576,7 @@ __global__ void __launch_bounds__(kDispatch ? kDispatchThreads : kThreads, 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * kBN;
       // row within the tile held by this lane (half tiles: lanes 0-15 of a quarter)
-      const int row_in_tile = tile_row_of_lane((v & kRingHalf) != 0, q, lane);
+      const int row_in_tile = tile_row_of_lane(half_tile(rows_valid), q, lane);
       const bool has_row = row_in_tile < rows_valid;
       const int64_t row = row0 + row_in_tile;
       if (tr.kind == 0) {
@@ -748,10 +703,9 @@ int expert_swiglu_fused(const void* xs, int64_t rows_cap, int64_t H, int64_t I,
   P.n_dn = static_cast<int>(ceil_div(H, kBN));
   P.kb_gu = static_cast<int>(ceil_div(H, kBK));
   P.kb_dn = static_cast<int>(ceil_div(I, kBK));
-  // A CTA holds up to about four tiles between claiming one and storing its output (two claimed
-  // ahead, one in its MMAs, one in its epilogue); a lag of twice that keeps down tiles from
-  // waiting for h even when epilogues run slow.
-  P.lag = static_cast<int>(std::max<int64_t>(1, ceil_div(8 * grid, P.n_gu + P.n_dn)));
+  // A CTA holds up to about three tiles between claiming one and storing its output; a lag of
+  // twice that keeps down tiles from waiting for h even when epilogues run slow.
+  P.lag = static_cast<int>(std::max<int64_t>(1, ceil_div(6 * grid, P.n_gu + P.n_dn)));
   P.wait_ns = wait_limit_ns();
   P.peer_wait_ns = peer_wait_limit_ns();
   P.H = H;
