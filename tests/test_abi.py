@@ -2,6 +2,7 @@
 (no GPU needed: nothing here launches a kernel)."""
 import ctypes
 import re
+from pathlib import Path
 
 import pytest
 
@@ -78,3 +79,24 @@ def test_controls_and_new_entry_points_check_arguments(lib):
     assert st == capi.ERR_ARG
     assert lib.prism_moe_ep_landing_bytes(65, 8, 2, 64, 8, capi.BF16) == 0    # > 64 ranks
     assert lib.prism_moe_ep_workspace_size(8, 64, 32, 9, 2, 2, capi.BF16) == 0   # E % W != 0
+
+
+def test_c_host_builds_links_and_runs(lib, tmp_path):
+    """The header compiles as C99 with every warning as an error, a C program links against the
+    library, and the calls that need no GPU behave as from Python."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    src = Path(__file__).resolve().parent / "c_host" / "abi_consumer.c"
+    inc = Path(__file__).resolve().parent.parent / "include"
+    libdir = capi.LIB_PATH.parent
+    exe = tmp_path / "abi_consumer"
+    subprocess.run([gcc, "-std=c99", "-Wall", "-Wextra", "-Werror", f"-I{inc}", str(src), "-o",
+                    str(exe), f"-L{libdir}", "-lprism_moe", f"-Wl,-rpath,{libdir}"],
+                   check=True, capture_output=True, text=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, r.stdout + r.stderr
+    lines = r.stdout.split("\n")
+    assert sum(1 for ln in lines if ln.startswith("ok ")) >= 15, r.stdout
